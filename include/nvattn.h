@@ -1,0 +1,126 @@
+/*
+ * nvattn.h — C ABI of the B200 (sm_100a) attention hot path for nano-vllm-spec-decode.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, element strides and sizes (no framework types);
+ *   - is asynchronous on the `stream` argument (a cudaStream_t passed as void*), makes no host
+ *     synchronisation and performs no device allocation, so it can be captured in a CUDA graph;
+ *   - returns an nva_status (0 = success). Invalid arguments are rejected before any launch.
+ *
+ * Tensor layouts follow nano-vllm (nanovllm/layers/attention.py):
+ *   q        [T_q, H, D]        bf16, head stride D, row stride q_row_stride (elements)
+ *   key/value[T, KVH, D]        bf16, head stride D, row stride *_row_stride (elements)
+ *   k_cache  [NB, BS, KVH, D]   bf16, contiguous (one layer's slice of the [2, L, NB, BS, KVH, D] pool)
+ *   block_tables [B, W]         int32, row stride bt_row_stride, -1 = unused
+ *   out      [T_q, H, D]        bf16, row stride out_row_stride (elements)
+ * Query head h reads kv head h / (H / KVH) (grouped-query attention).
+ */
+#ifndef NVATTN_H
+#define NVATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NVA_API __attribute__((visibility("default")))
+
+typedef enum {
+  NVA_OK = 0,
+  NVA_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, shape mismatch */
+  NVA_ERR_UNSUPPORTED = 2,      /* a shape or dtype the kernels do not implement (e.g. head_dim != 128) */
+  NVA_ERR_ALIGNMENT = 3,        /* pointer or stride not 16-byte aligned where the kernel needs it */
+  NVA_ERR_WORKSPACE = 4,        /* workspace pointer null or smaller than *_workspace_bytes() */
+  NVA_ERR_CUDA = 5,             /* a CUDA runtime/driver call failed (launch error, no device) */
+} nva_status;
+
+/* Library version, (major << 16) | minor. */
+NVA_API int nva_version(void);
+
+/* Static description of an nva_status value. */
+NVA_API const char* nva_status_string(int status);
+
+/* Text of the last CUDA error seen by this thread inside the library ("" if none). */
+NVA_API const char* nva_last_cuda_error(void);
+
+/*
+ * (a) KV scatter.  Replaces store_kvcache / store_kvcache_kernel (nanovllm/layers/attention.py:10-40).
+ * For every token i with slot = slot_mapping[i] != -1:
+ *     k_cache.flat[slot * row_elems + j] = key[i * key_row_stride + j]   for j < row_elems
+ * and the same for value/v_cache, where row_elems = num_kv_heads * head_dim.  Bit copy: any 2- or 4-byte
+ * element type.  Slots outside [0, num_slots) are skipped and recorded in the device error word.
+ */
+NVA_API int nva_store_kvcache(const void* key, int64_t key_row_stride, const void* value, int64_t value_row_stride,
+                              void* k_cache, void* v_cache, int64_t num_slots, const int32_t* slot_mapping,
+                              int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim, int32_t elem_bytes,
+                              void* stream);
+
+/*
+ * (b)+(c) Paged decode / speculative-verify attention.  Replaces flash_attn_with_kvcache as called from
+ * Attention.forward's decode branch (nanovllm/layers/attention.py:71-78):
+ *     q [num_seqs, q_per_seq, H, D] -> out [num_seqs, q_per_seq, H, D], causal, bottom-right aligned:
+ *     query i of sequence b attends to cache positions [0, context_lens[b] - q_per_seq + i].
+ * context_lens include the q_per_seq new tokens (already stored by nva_store_kvcache).  A sequence with
+ * context length 0 (batch padding) reads nothing and gets a zero output.  q_per_seq * (H / KVH) <= 48.
+ * Requires head_dim 128, bf16, block_size a multiple of 128.  workspace >= nva_paged_decode_workspace_bytes().
+ */
+NVA_API int nva_paged_decode(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+                             int32_t num_blocks, int32_t block_size, const int32_t* context_lens,
+                             const int32_t* block_tables, int32_t bt_row_stride, int32_t num_seqs, int32_t q_per_seq,
+                             int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float softmax_scale,
+                             void* out, int64_t out_row_stride, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+NVA_API size_t nva_paged_decode_workspace_bytes(int32_t num_seqs, int32_t q_per_seq, int32_t num_heads,
+                                                int32_t num_kv_heads, int32_t head_dim);
+
+/*
+ * (d) Varlen causal attention for prefill and mixed prefill+decode batches.  Replaces flash_attn_varlen_func
+ * as called from Attention.forward's prefill branch (nanovllm/layers/attention.py:64-70).
+ * Sequence b owns query rows [cu_seqlens_q[b], cu_seqlens_q[b+1]) and keys [0, Lk_b) with
+ * Lk_b = cu_seqlens_k[b+1] - cu_seqlens_k[b]; query row i of the sequence attends to keys [0, Lk_b - Lq_b + i].
+ * Keys/values come from the paged cache through block_tables when block_tables != NULL (prefix cache,
+ * chunked prefill, mixed batches), else from the contiguous key/value tensors at rows cu_seqlens_k[b] + pos.
+ * max_seqlen_q / max_seqlen_k are upper bounds only (they size nothing on the device).
+ * Requires head_dim 128, bf16.  workspace >= nva_varlen_workspace_bytes().
+ */
+NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void* key, int64_t key_row_stride,
+                                 const void* value, int64_t value_row_stride, const void* k_cache,
+                                 const void* v_cache, int32_t num_blocks, int32_t block_size,
+                                 const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t num_seqs,
+                                 int32_t total_q, int32_t total_k, int32_t max_seqlen_q, int32_t max_seqlen_k,
+                                 const int32_t* block_tables, int32_t bt_row_stride, int32_t num_heads,
+                                 int32_t num_kv_heads, int32_t head_dim, float softmax_scale, void* out,
+                                 int64_t out_row_stride, void* workspace, size_t workspace_bytes, void* stream);
+
+NVA_API size_t nva_varlen_workspace_bytes(int32_t num_seqs, int32_t total_q, int32_t num_heads,
+                                          int32_t num_kv_heads, int32_t head_dim);
+
+/*
+ * (c) Greedy accept length.  Replaces the greedy core of verify_drafts (nanovllm/layers/sampler.py:66-82) on
+ * already-reduced target ids (row argmaxes of the verify logits):
+ *     accepted[s, j] = target[s, j] == draft[s, j] && j < num_drafts[s]
+ *     num_accepted[s] = length of the unbroken run of accepts from j = 0
+ *     next_token[s]   = target[s, num_accepted[s]]
+ * target [S, K+1], draft [S, K] (row strides in elements), num_drafts [S]; ids and outputs are int32 when
+ * id_bytes == 4, int64 when id_bytes == 8 (num_drafts and num_accepted use the same width).  K may be 0.
+ */
+NVA_API int nva_greedy_accept(const void* target_ids, int64_t target_row_stride, const void* draft_ids,
+                              int64_t draft_row_stride, const void* num_drafts, int32_t num_seqs, int32_t k,
+                              int32_t id_bytes, void* num_accepted, void* next_tokens, void* stream);
+
+/*
+ * Device error word.  Kernels never trap: a slot or block id out of range, or a pipeline wait that ran past its
+ * time limit, sets a bit here and the kernel skips the access or returns.  Reading it synchronises the device.
+ * Bits: 1 = scatter slot out of range, 2 = pipeline wait timed out, 4 = block id out of range.
+ */
+NVA_API int nva_get_device_error(uint32_t* out_bits);
+NVA_API int nva_clear_device_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVATTN_H */

@@ -1,0 +1,79 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.  Not part of the public header.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+namespace nva {
+
+constexpr int kHeadDim = 128;
+constexpr int kTileTokens = 128;      // KV tokens per pipeline stage (= UMMA M)
+constexpr int kMaxDecodeSeqs = 1024;  // sequences the decode kernel's on-chip schedule holds
+constexpr int kMaxDecodeRows = 48;    // q_per_seq * group rows per kv head (UMMA N)
+
+// One attention step over paged KV, seen from the decode / verify kernel.  Two modes:
+//   decode  (cu_q == nullptr): sequence b owns q rows [b*n_fixed, (b+1)*n_fixed), keys [0, ctx_lens[b]);
+//   varlen  (cu_q != nullptr): rows [cu_q[b], cu_q[b+1]), keys [0, cu_k[b+1]-cu_k[b]); only sequences with
+//           1 <= q_len <= max_n are handled here (longer ones go to the prefill kernel).
+struct DecodeParams {
+  const __nv_bfloat16* q;
+  int64_t q_row_stride;
+  __nv_bfloat16* out;
+  int64_t out_row_stride;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  const int32_t* ctx_lens;
+  const int32_t* block_tables;
+  int32_t bt_stride;
+  int32_t num_seqs;
+  int32_t n_fixed;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t group;
+  int32_t max_n;
+  int32_t block_size;
+  int32_t num_blocks;
+  float scale_log2;
+  float* part_o;     // [2 * grid, NP, 128] split partial outputs (normalised)
+  float* part_lse;   // [2 * grid, NP] their log2-sum-exp
+};
+
+size_t decode_workspace_bytes(int grid, int np);
+int decode_rows_padded(int rows);  // 16, 32 or 48 (0 if too many)
+cudaError_t launch_paged_decode(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const DecodeParams& p, int np,
+                                int grid, cudaStream_t stream);
+
+// Varlen prefill kernel (long query runs) — q rows tiled by 128 per (sequence, q head).
+struct PrefillParams {
+  const __nv_bfloat16* q;
+  int64_t q_row_stride;
+  __nv_bfloat16* out;
+  int64_t out_row_stride;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  const int32_t* block_tables;  // nullptr: contiguous K/V rows cu_k[b] + pos
+  int32_t bt_stride;
+  int32_t num_seqs;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t group;
+  int32_t min_q;                // sequences with q_len >= min_q are handled here
+  int32_t block_size;
+  int32_t num_blocks;
+  int32_t q_tiles_bound;        // grid.x: upper bound on the number of 128-row q tiles
+  float scale_log2;
+};
+cudaError_t launch_prefill(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                           const PrefillParams& p, cudaStream_t stream);
+
+cudaError_t launch_store_kvcache(const void* key, int64_t key_row_stride, const void* value,
+                                 int64_t value_row_stride, void* k_cache, void* v_cache, int64_t num_slots,
+                                 const int32_t* slots, int32_t num_tokens, int32_t row_elems, int32_t elem_bytes,
+                                 cudaStream_t stream);
+
+cudaError_t launch_greedy_accept(const void* target, int64_t target_row_stride, const void* drafts,
+                                 int64_t draft_row_stride, const void* num_drafts, int32_t num_seqs, int32_t k,
+                                 int32_t id_bytes, void* num_accepted, void* next_tokens, cudaStream_t stream);
+
+}  // namespace nva

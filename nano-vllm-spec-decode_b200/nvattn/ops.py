@@ -1,0 +1,131 @@
+"""Torch-facing wrappers over the C ABI, with the signatures of the calls nano-vllm makes on its attention path.
+
+  store_kvcache(key, value, k_cache, v_cache, slot_mapping)        nanovllm/layers/attention.py:33-40
+  flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens=, block_table=, softmax_scale=, causal=True)
+                                                                    flash-attn call at attention.py:75-77
+  flash_attn_varlen_func(q, k, v, max_seqlen_q=, cu_seqlens_q=, max_seqlen_k=, cu_seqlens_k=, softmax_scale=,
+                         causal=True, block_table=)                 flash-attn call at attention.py:67-70
+  greedy_accept(target_ids, draft_ids, num_drafts)                  greedy core of verify_drafts, sampler.py:66-82
+
+Every op runs on the caller's current CUDA stream, allocates only its output (and, for attention, a workspace
+from torch's caching allocator, which comes from the graph pool under CUDA-graph capture) and never syncs.
+There is no CPU path: non-CUDA tensors raise.
+"""
+import torch
+
+from . import _lib
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("nvattn ops run on CUDA tensors only (no CPU fallback)")
+
+
+def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  slot_mapping: torch.Tensor) -> None:
+    """Scatter this step's K/V rows into the paged cache (attention.py:33-40; same asserts)."""
+    N, num_heads, head_dim = key.shape
+    D = num_heads * head_dim
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    assert key.stride(1) == head_dim and value.stride(1) == head_dim
+    assert k_cache.stride(1) == D and v_cache.stride(1) == D
+    assert slot_mapping.numel() == N
+    _need_cuda(key, value, k_cache, v_cache, slot_mapping)
+    assert key.dtype == value.dtype == k_cache.dtype == v_cache.dtype
+    assert k_cache.is_contiguous() and v_cache.is_contiguous()
+    assert slot_mapping.dtype == torch.int32 and slot_mapping.is_contiguous()
+    num_slots = k_cache.numel() // D
+    _lib.check(_lib.load().nva_store_kvcache(
+        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+        num_slots, slot_mapping.data_ptr(), N, num_heads, head_dim, key.element_size(), _stream()),
+        "store_kvcache")
+
+
+def flash_attn_with_kvcache(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, cache_seqlens: torch.Tensor,
+                            block_table: torch.Tensor, softmax_scale: float, causal: bool = True,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+    """Paged decode / verify attention.  q [B, n, H, D] bf16; k_cache/v_cache [NB, BS, KVH, D]; cache_seqlens
+    [B] int32 (including the n new tokens); block_table [B, W] int32.  Causal, bottom-right aligned."""
+    assert causal, "nano-vllm always calls with causal=True"
+    B, n, H, D = q.shape
+    NB, BS, KVH, _ = k_cache.shape
+    _need_cuda(q, k_cache, v_cache, cache_seqlens, block_table)
+    assert q.dtype == k_cache.dtype == v_cache.dtype == torch.bfloat16
+    assert q.stride(-1) == 1 and q.stride(2) == D and q.stride(0) == n * q.stride(1)
+    assert k_cache.is_contiguous() and v_cache.is_contiguous()
+    assert cache_seqlens.dtype == torch.int32 and cache_seqlens.is_contiguous() and cache_seqlens.numel() == B
+    assert block_table.dtype == torch.int32 and block_table.stride(-1) == 1 and block_table.shape[0] == B
+    if out is None:
+        out = torch.empty(B, n, H, D, dtype=q.dtype, device=q.device)
+    lib = _lib.load()
+    ws_bytes = lib.nva_paged_decode_workspace_bytes(B, n, H, KVH, D)
+    if ws_bytes == 0:
+        raise _lib.NvattnError(f"paged decode does not support q_per_seq={n} with {H // KVH} q heads per kv head")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    _lib.check(lib.nva_paged_decode(
+        q.data_ptr(), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), NB, BS, cache_seqlens.data_ptr(),
+        block_table.data_ptr(), block_table.stride(0), B, n, H, KVH, D, float(softmax_scale), out.data_ptr(),
+        out.stride(1), ws.data_ptr(), ws_bytes, _stream()), "paged decode")
+    return out
+
+
+def flash_attn_varlen_func(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, max_seqlen_q: int,
+                           cu_seqlens_q: torch.Tensor, max_seqlen_k: int, cu_seqlens_k: torch.Tensor,
+                           softmax_scale: float, causal: bool = True, block_table: torch.Tensor | None = None,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+    """Varlen causal attention.  q [Tq, H, D]; with block_table, k/v are the paged caches [NB, BS, KVH, D],
+    else contiguous [Tk, KVH, D] rows (any row stride).  max_seqlen_* are upper bounds only."""
+    assert causal, "nano-vllm always calls with causal=True"
+    Tq, H, D = q.shape
+    _need_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k, block_table)
+    assert q.dtype == k.dtype == v.dtype == torch.bfloat16
+    assert q.stride(-1) == 1 and q.stride(1) == D
+    assert cu_seqlens_q.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32
+    assert cu_seqlens_q.is_contiguous() and cu_seqlens_k.is_contiguous()
+    B = cu_seqlens_q.numel() - 1
+    if out is None:
+        out = torch.empty(Tq, H, D, dtype=q.dtype, device=q.device)
+    lib = _lib.load()
+    if block_table is not None:
+        NB, BS, KVH, _ = k.shape
+        assert k.is_contiguous() and v.is_contiguous()
+        assert block_table.dtype == torch.int32 and block_table.stride(-1) == 1
+        kp, kst, vp, vst, Tk = 0, 0, 0, 0, 0
+        kc, vc, bt, bts = k.data_ptr(), v.data_ptr(), block_table.data_ptr(), block_table.stride(0)
+    else:
+        Tk, KVH, _ = k.shape
+        assert k.stride(-1) == 1 and k.stride(1) == D and v.stride(-1) == 1 and v.stride(1) == D
+        NB, BS = 0, 0
+        kp, kst, vp, vst = k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0)
+        kc, vc, bt, bts = 0, 0, 0, 0
+    ws_bytes = lib.nva_varlen_workspace_bytes(B, Tq, H, KVH, D)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
+    _lib.check(lib.nva_varlen_attention(
+        q.data_ptr(), q.stride(0), kp, kst, vp, vst, kc, vc, NB, BS, cu_seqlens_q.data_ptr(),
+        cu_seqlens_k.data_ptr(), B, Tq, Tk, int(max_seqlen_q), int(max_seqlen_k), bt, bts, H, KVH, D,
+        float(softmax_scale), out.data_ptr(), out.stride(0), ws.data_ptr(), ws_bytes, _stream()), "varlen attention")
+    return out
+
+
+def greedy_accept(target_ids: torch.Tensor, draft_ids: torch.Tensor, num_drafts: torch.Tensor):
+    """Integer greedy accept length: target [S, K+1], drafts [S, K], num_drafts [S] (all int32 or all int64).
+    Returns (num_accepted [S], next_token [S]) in the same dtype."""
+    _need_cuda(target_ids, draft_ids, num_drafts)
+    S, K1 = target_ids.shape
+    K = K1 - 1
+    dt = target_ids.dtype
+    assert dt in (torch.int32, torch.int64) and draft_ids.dtype == dt and num_drafts.dtype == dt
+    assert target_ids.stride(-1) == 1 and num_drafts.is_contiguous() and num_drafts.numel() == S
+    assert draft_ids.shape == (S, K) and (K == 0 or draft_ids.stride(-1) == 1)
+    acc = torch.empty(S, dtype=dt, device=target_ids.device)
+    nxt = torch.empty(S, dtype=dt, device=target_ids.device)
+    _lib.check(_lib.load().nva_greedy_accept(
+        target_ids.data_ptr(), target_ids.stride(0), draft_ids.data_ptr() if K else 0, draft_ids.stride(0) if K else 0,
+        num_drafts.data_ptr(), S, K, target_ids.element_size(), acc.data_ptr(), nxt.data_ptr(), _stream()),
+        "greedy accept")
+    return acc, nxt
