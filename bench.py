@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""Benchmark of the attention hot path (BASELINE metric: decode/verify attention HBM GB/s, prefill TFLOP/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nvattn|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N ...
+
+Headline workload: BASELINE config 2 (Qwen3-8B paged decode: 32 q / 8 kv heads, head_dim 128, block 256,
+context U[512, 4096]).  A step is one Attention.forward of the decode branch over the batch: the KV scatter of
+the new tokens plus paged decode attention.  Multi-GPU follows nano-vllm's tensor-parallel head split: rank r
+owns kv heads [r*8/N, (r+1)*8/N) and their q heads, for a global batch of 64*N sequences (weak scaling: every
+rank reads the same ~640 MB of KV per step as one GPU does at N=1).  No collective runs inside attention; the
+only NCCL calls are the barrier and the max-over-ranks of the timings.
+
+value      algorithmic bytes (KV read once per kv head + q + o + the scatter's read and write) of all ranks,
+           divided by the slowest rank's device time (CUDA events), inputs resident in HBM, L2 flushed between
+           timed steps by a 256 MiB write outside the events.
+e2e        the same bytes through the public nvattn.attention.Attention.forward with the step's inputs copied
+           host->device from pinned memory and the output copied back inside the timed region.
+roofline   the decode launch (main kernel + split combine) timed alone with CUDA events vs measured HBM peak.
+The reference arm (--impl reference) times the reference semantics (the FP32 torch oracle) on host cores.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "nano-vllm-spec-decode_b200"))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+GiB = 1 << 30
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return dict(hbm=float(d["hbm_gbs"]), bf16=float(d["bf16_tflops"]),
+                    bf16_sustained=float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), source="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
+
+
+def traffic_summary():
+    path = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        self.gpu_index = gpu_index
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu_index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.3)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+                self.lines = [l for l in out.splitlines() if l.strip()]
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------------------------------------- work
+def decode_shard(world, rank, seed=0, B_per_gpu=64, k=0):
+    """This rank's KV-head shard of the (weak-scaled) decode / verify batch."""
+    from nvattn.workloads import paged_decode_batch
+    B = B_per_gpu * world
+    g = torch.Generator().manual_seed(seed)
+    if k == 0:
+        lens = torch.randint(512, 4097, (B,), generator=g).tolist()
+    else:
+        lens = torch.randint(256, 2049, (B,), generator=g).tolist()
+    H, KVH = 32 // world, 8 // world
+    b = paged_decode_batch(lens, k + 1, H, KVH, 128, 2048 * world, 0.5, seed + 1 + rank, device="cuda",
+                           device_fill=True)
+    return b, lens, H, KVH
+
+
+def attn_bytes(lens, n, H, KVH):
+    from nvattn.workloads import bytes_decode
+    return bytes_decode(lens, n, H, KVH)
+
+
+def scatter_bytes(T, KVH):
+    return 2.0 * T * KVH * 128 * 2 * 2     # k and v rows, read + write
+
+
+def capture(fn):
+    """CUDA graph of fn (warmed up on a side stream first), the way nano-vllm replays its decode steps."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def time_steps(fn, steps, warmup, flush):
+    """Per-step device time (ms) with CUDA events on the current stream; L2 flushed before each step outside the
+    events.  Returns the list of step times."""
+    for _ in range(warmup):
+        flush.zero_()
+        fn()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record()
+        fn()
+        ends[i].record()
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def run_nvattn(args, world, rank, local):
+    from nvattn import ops
+    from nvattn.attention import Attention
+    from nvattn.context import set_context, reset_context
+    pk = peaks()
+    b, lens, H, KVH = decode_shard(world, rank, args.seed)
+    B = b.num_seqs
+    q4 = b.q.view(B, 1, H, 128)
+    out = torch.empty_like(q4)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    a_bytes = attn_bytes(lens, 1, H, KVH)
+    s_bytes = scatter_bytes(B, KVH)
+
+    def step():
+        ops.store_kvcache(b.k_new, b.v_new, b.k_cache, b.v_cache, b.slot_mapping)
+        ops.flash_attn_with_kvcache(q4, b.k_cache, b.v_cache, cache_seqlens=b.context_lens,
+                                    block_table=b.block_tables, softmax_scale=b.scale, out=out)
+
+    def attn_only():
+        ops.flash_attn_with_kvcache(q4, b.k_cache, b.v_cache, cache_seqlens=b.context_lens,
+                                    block_table=b.block_tables, softmax_scale=b.scale, out=out)
+
+    g_step = capture(step)
+    g_attn = capture(attn_only)
+
+    # ---- headline: device-resident inputs, one graph replay (scatter + attention) per step
+    barrier(world)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        times = time_steps(g_step.replay, args.steps, args.warmup, flush)
+        barrier(world)
+    total_ms = max_over_ranks(sum(times), world)
+    ms_step = total_ms / args.steps
+    value = world * (a_bytes + s_bytes) / (ms_step * 1e-3) / 1e9
+
+    # ---- roofline: the decode launch alone
+    k_times = time_steps(g_attn.replay, args.steps, args.warmup, flush)
+    k_ms = max_over_ranks(statistics.mean(k_times), world)
+    achieved = a_bytes / (k_ms * 1e-3) / 1e9
+    tr = traffic_summary().get("paged_decode_config2")
+    traffic = None
+    if tr:
+        # per-launch DRAM bytes of the captured case, scaled by the KV bytes this launch reads
+        traffic = tr["dram_bytes"] * (a_bytes / tr["algorithmic_bytes"])
+
+    # ---- e2e through the public Attention.forward with host buffers
+    attn = Attention(H, 128, b.scale, KVH)
+    attn.k_cache, attn.v_cache = b.k_cache, b.v_cache
+    host = {n: t.cpu().pin_memory() for n, t in dict(q=b.q, k=b.k_new, v=b.v_new, slots=b.slot_mapping,
+                                                      ctx=b.context_lens, bt=b.block_tables).items()}
+    dev = {n: torch.empty_like(t, device="cuda") for n, t in host.items()}
+    out_host = torch.empty(B, H, 128, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    # Attention.forward captured once over static device buffers (ModelRunner.capture_cudagraph); each step copies
+    # the step's inputs in from pinned host memory, replays, and copies the output back (ModelRunner.run_model).
+    for n in host:
+        dev[n].copy_(host[n])
+    set_context(False, slot_mapping=dev["slots"], context_lens=dev["ctx"], block_tables=dev["bt"])
+    o_static = {}
+
+    def fwd():
+        o_static["o"] = attn(dev["q"], dev["k"], dev["v"])
+    g_fwd = capture(fwd)
+    reset_context()
+
+    def e2e_step():
+        for n in host:
+            dev[n].copy_(host[n], non_blocking=True)
+        g_fwd.replay()
+        out_host.copy_(o_static["o"], non_blocking=True)
+
+    barrier(world)
+    e_times = time_steps(e2e_step, args.steps, args.warmup, flush)
+    e_ms = max_over_ranks(sum(e_times), world) / args.steps
+    e2e_value = world * (a_bytes + s_bytes) / (e_ms * 1e-3) / 1e9
+
+    # ---- secondary rows: verify (config 3) and greedy accept at this N
+    secondary = {}
+    for k in (1, 2, 4, 8):
+        vb, vl, _, _ = decode_shard(world, rank, args.seed + 10 + k, B_per_gpu=32, k=k)
+        vq = vb.q.view(vb.num_seqs, k + 1, H, 128)
+        vout = torch.empty_like(vq)
+
+        def vstep():
+            ops.flash_attn_with_kvcache(vq, vb.k_cache, vb.v_cache, cache_seqlens=vb.context_lens,
+                                        block_table=vb.block_tables, softmax_scale=vb.scale, out=vout)
+        vt = time_steps(capture(vstep).replay, max(10, args.steps // 2), args.warmup, flush)
+        v_ms = max_over_ranks(statistics.mean(vt), world)
+        vbytes = attn_bytes(vl, k + 1, H, KVH)
+        from nvattn.workloads import flops_decode
+        secondary[f"verify_k{k}"] = {"GBps": round(world * vbytes / (v_ms * 1e-3) / 1e9, 1),
+                                     "frac_hbm": round(vbytes / (v_ms * 1e-3) / 1e9 / pk["hbm"], 3),
+                                     "us": round(v_ms * 1e3, 2),
+                                     "TFLOPs": round(world * flops_decode(vl, k + 1, H) / (v_ms * 1e-3) / 1e12, 1)}
+        del vb, vq, vout
+    from nvattn.workloads import accept_config
+    t_ids, d_ids, nd = (x.cuda() for x in accept_config(8, S=32, seed=args.seed))
+    acc_out = {}
+
+    def accept():
+        acc_out["r"] = ops.greedy_accept(t_ids, d_ids, nd)
+    at = time_steps(capture(accept).replay, 50, 5, flush)
+    secondary["greedy_accept_k8_S32_us"] = round(statistics.median(at) * 1e3, 2)
+
+    line = {
+        "metric": "decode attention HBM GB/s (BASELINE config 2: Qwen3-8B paged decode)",
+        "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded; BASELINE config 2 shapes)",
+        "config": {"workload": "paged decode step = KV scatter + GQA paged attention, BASELINE config 2",
+                   "timing": "CUDA-graph replay per step, CUDA events, max over ranks",
+                   "global_batch": B, "per_rank_q_heads": H, "per_rank_kv_heads": KVH, "head_dim": 128,
+                   "block_size": 256, "context": "U[512, 4096]", "parallelism": f"kv-head shards x{world}",
+                   "l2": "flushed between timed steps (256 MiB write outside the events)"},
+        "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e_ms, 5),
+                "api": "nvattn.attention.Attention.forward (CUDA-graph replay, inputs H2D from pinned memory, output D2H)"},
+        "roofline": {"kernel": "paged_decode_kernel<16> + paged_decode_combine", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": pk["hbm"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm"], 4), "peak_source": pk["source"],
+                     "traffic": None if traffic is None else round(traffic),
+                     "algorithmic_bytes": round(a_bytes), "us": round(k_ms * 1e3, 2)},
+        "gpu_launches": 3 * args.steps,
+        "secondary": secondary,
+    }
+    clocks = clk.summary()
+    line["clocks"] = clocks
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.seed, budget_s=args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def cpu_sample(seed, nseq):
+    """The first nseq sequences of the config-2 batch, generated on the CPU (same lengths as the GPU run)."""
+    from nvattn.workloads import paged_decode_batch
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(512, 4097, (64,), generator=g).tolist()[:nseq]
+    nblk = sum((L + 255) // 256 for L in lens)
+    b = paged_decode_batch(lens, 1, 32, 8, 128, nblk, 0.5, seed + 1, device="cpu")
+    return b, lens
+
+
+def time_oracle(b, lens, reps):
+    import oracle
+    q = b.q.view(len(lens), 1, 32, 128)
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oracle.paged_attention_ref(q, b.k_cache, b.v_cache, b.context_lens, b.block_tables, b.scale)
+        best = min(best, time.perf_counter() - t0)
+    return best
+
+
+def cpu_baseline(seed, budget_s=10.0):
+    """The FP32 torch restatement of the reference semantics (oracle.paged_attention_ref) on host cores, on a
+    bounded sample of the config-2 batch; same metric (algorithmic bytes / s)."""
+    b, lens = cpu_sample(seed, 1)
+    t1 = time_oracle(b, lens, 1)
+    nseq = max(1, min(64, int(budget_s / 3 / max(t1, 1e-3))))
+    b, lens = cpu_sample(seed, nseq)
+    best = time_oracle(b, lens, 3)
+    by = attn_bytes(lens, 1, 32, 8)
+    return {"value": round(by / best / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"first {nseq} of the 64 config-2 sequences ({sum(lens)} tokens), best of 3, FP32 torch oracle",
+            "host_cpu_count": os.cpu_count()}
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the reference semantics on the host cores (FP32 torch oracle), same metric and config."""
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    b, lens = cpu_sample(args.seed, 2)
+    by = attn_bytes(lens, 1, 32, 8)
+    import oracle
+    q = b.q.view(len(lens), 1, 32, 128)
+    for _ in range(max(1, min(args.warmup, 3))):
+        oracle.paged_attention_ref(q, b.k_cache, b.v_cache, b.context_lens, b.block_tables, b.scale)
+    steps = max(1, min(args.steps, 20))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.paged_attention_ref(q, b.k_cache, b.v_cache, b.context_lens, b.block_tables, b.scale)
+    dt = (time.perf_counter() - t0) / steps
+    value = by / dt / 1e9
+    sample = f"first 2 of the 64 config-2 sequences ({sum(lens)} tokens) per step, {steps} steps"
+    line = {"impl": "reference", "metric": "decode attention HBM GB/s (BASELINE config 2: Qwen3-8B paged decode)",
+            "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded; BASELINE config 2 shapes)",
+            "config": {"workload": "paged decode attention, BASELINE config 2 (sampled)", "global_batch": 2,
+                       "parallelism": "host cores"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["nvattn", "reference"], default="nvattn")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup()
+    assert world == args.gpus or "WORLD_SIZE" not in os.environ, "--gpus must match the launcher's world size"
+    assert 8 % world == 0, "kv heads (8) must split evenly across ranks"
+    try:
+        run_nvattn(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

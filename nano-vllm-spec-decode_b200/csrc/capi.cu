@@ -143,7 +143,8 @@ NVA_API int nva_paged_decode(const void* q, int64_t q_row_stride, const void* k_
     return NVA_ERR_INVALID_ARGUMENT;
   if (q_row_stride < static_cast<int64_t>(num_heads) * head_dim || out_row_stride < static_cast<int64_t>(num_heads) * head_dim)
     return NVA_ERR_INVALID_ARGUMENT;
-  if (!aligned16(q) || (q_row_stride % 8) != 0) return NVA_ERR_ALIGNMENT;
+  if (!aligned16(q) || (q_row_stride % 8) != 0 || !aligned16(out) || (out_row_stride % 8) != 0)
+    return NVA_ERR_ALIGNMENT;
   const int group = num_heads / num_kv_heads;
   const int np = nva::decode_rows_padded(q_per_seq * group);
   if (np == 0) return NVA_ERR_UNSUPPORTED;

@@ -2,21 +2,26 @@
 // nanovllm/layers/attention.py:75-77 and the short-query rows of flash_attn_varlen_func in mixed batches).
 //
 // Orientation ("swap AB"): the 128 tokens of a KV tile sit on the 128 TMEM lanes (UMMA M) and the query rows of
-// one kv head -- q_len draft positions x group q heads, packed row r = i * group + h -- sit on UMMA N (16/32/48).
-//   S^T[tok, r] = K[tok, :] . Q[r, :]        (A = K tile, K-major;  B = Q rows, K-major)
-//   O^T[d, r]   = sum_tok V[tok, d] P[tok, r] (A = V tile, MN-major; B = P^T, K-major)
+// one kv head -- q_len draft positions x group q heads, packed row r = i * group + h -- sit on UMMA N (16/32/48):
+//   S^T[tok, r] = K[tok, :] . Q[r, :]          A = K tile (K-major, 128B swizzle, straight from TMA)
+//                                              B = Q rows (K-major, 128B swizzle, gathered with cp.async)
+//   O^T[d, r]   = sum_tok V[tok, d] P[tok, r]   A = V tile (MN-major, 128B swizzle, straight from TMA)
+//                                              B = P^T    (MN-major, no swizzle, 16-byte stores per thread)
 // so one HBM pass over each KV block serves every q head of its group and every draft position.
 //
 // Work split: every CTA is persistent (one per SM) and owns an equal share of the 128-token tiles of all
-// (sequence, kv head) segments, in (sequence, kv head, tile) order.  A segment that lies inside one CTA is
-// finished there; one cut by a CTA boundary leaves a normalised partial + log2-sum-exp per piece, merged by
-// paged_decode_combine.  The split depends only on the batch's lengths, so padding sequences (length 0) change
-// nothing, and no host value or device read-back is involved (graph-capturable, fixed launch geometry).
+// (sequence, kv head) segments, in (sequence, kv head, tile) order.  A segment inside one CTA is finished there;
+// one cut by a CTA boundary leaves a normalised partial + log2-sum-exp per piece, merged by paged_decode_combine.
+// The split depends only on the batch's lengths (padding sequences of length 0 change nothing), and there is no
+// host value or device read-back involved: graph-capturable with a fixed launch geometry.
 //
-// Warp roles (256 threads): 0 = TMA producer (K and V tiles, 4 boxes of 64 dims x 128 tokens per stage),
-// 1 = TMEM owner + single-thread UMMA issuer, 2 = Q loader (gathers a segment's rows into the 128B-swizzled
-// operand layout), 3 = idle, 4..7 = softmax / accumulation (thread ct owns TMEM lane ct: token ct of S^T and
-// dim ct of O^T).
+// Warp roles (256 threads):
+//   0 = K producer, 3 = V producer: block-table ids prefetched 32 tiles at a time, then TMA 64 dims x 128 tokens
+//       boxes into 3-stage rings; K slots are released right after S = K Q^T, V slots after the PV product;
+//   1 = TMEM owner + UMMA issuer: polls the ring / softmax barriers and issues whichever product is ready;
+//   2 = Q loader: gathers a segment's rows into the swizzled operand layout (cp.async, zero-filled padding);
+//   4..7 = softmax: thread ct owns TMEM lane ct (token ct of S^T, dim ct of O^T).  Column maxima and sums over
+//       the 128 tokens use a transposed butterfly (each shuffle stage halves the rows a lane carries).
 #include "nva_ptx.cuh"
 #include "nva_kernels.h"
 
@@ -25,35 +30,42 @@ namespace nva {
 namespace {
 
 constexpr int kStages = 3;
-constexpr int kSlab = 128 * 128;            // 128 rows x 128 bytes
-constexpr int kStageBytes = 4 * kSlab;      // K lo, K hi, V lo, V hi
+constexpr int kSlab = 128 * 128;        // 128 rows x 128 bytes (64 bf16 dims)
+constexpr int kTileBytes = 2 * kSlab;   // one K or V tile: dims 0-63 and 64-127
 constexpr int kThreads = 256;
-constexpr int kConsumerBase = 128;          // first softmax thread
+constexpr int kConsumerBase = 128;
 constexpr float kNegInf = -__builtin_huge_valf();
+constexpr uint32_t kFull = 0xffffffffu;
+// Tile descriptors travel from the K producer to the MMA and softmax warps through a ring of this depth.  The
+// producer runs at most kStages tiles ahead of the S products and those at most 2 ahead of the softmax warps, so
+// an entry is never rewritten before the softmax warps have read it.
+constexpr int kInfoRing = 8;
 
 template <int NP>
-struct Smem {
-  static constexpr int kQ = kStages * kStageBytes;
-  static constexpr int kP = kQ + NP * 256;
-  static constexpr int kMisc = kP + NP * 256;
-  // misc block
-  static constexpr int kBars = kMisc;                         // 16 x u64
-  static constexpr int kInfo = kBars + 16 * 8;                // kStages x int4
-  static constexpr int kRed = kInfo + kStages * 16;           // [2][4][NP] float
-  static constexpr int kM = kRed + 2 * 4 * NP * 4;            // [NP]
-  static constexpr int kAlpha = kM + NP * 4;                  // [2][NP]
-  static constexpr int kLred = kAlpha + 2 * NP * 4;           // [4][NP]
-  static constexpr int kTmem = kLred + 4 * NP * 4;            // u32
-  static constexpr int kAbort = kTmem + 4;                    // int
-  static constexpr int kScan = kAbort + 4;                    // [8] int (warp totals)
-  static constexpr int kPrefix = kScan + 8 * 4;               // [kMaxDecodeSeqs + 1] int
+struct Cfg {
+  static constexpr int kQBuf = NP <= 32 ? 2 : 1;                 // Q double-buffered when shared memory allows
+  static constexpr int kK = 0;                                   // K ring
+  static constexpr int kV = kStages * kTileBytes;                // V ring
+  static constexpr int kQ = 2 * kStages * kTileBytes;            // Q buffers, NP * 256 bytes each
+  static constexpr int kP = kQ + kQBuf * NP * 256;               // P^T, NP * 256 bytes
+  static constexpr int kBars = kP + NP * 256;                    // 32 x u64
+  static constexpr int kInfo = kBars + 32 * 8;                   // kInfoRing x 2 x int4
+  static constexpr int kRed = kInfo + kInfoRing * 32;            // [2][4][NP] column maxima per warp
+  static constexpr int kM = kRed + 2 * 4 * NP * 4;               // [NP] running max
+  static constexpr int kAlpha = kM + NP * 4;                     // [2][NP] rescale factors
+  static constexpr int kLred = kAlpha + 2 * NP * 4;              // [4][NP] column sums per warp
+  static constexpr int kTmem = kLred + 4 * NP * 4;
+  static constexpr int kAbort = kTmem + 4;
+  static constexpr int kScan = kAbort + 4;                       // [8]
+  static constexpr int kPrefix = kScan + 32;                     // [kMaxDecodeSeqs + 1]
   static constexpr int kEnd = kPrefix + (kMaxDecodeSeqs + 1) * 4;
-  static constexpr int kBytes = kEnd + 1024;                  // + slack for 1024-byte alignment
+  static constexpr int kBytes = kEnd + 1024;                     // + slack for 1024-byte alignment
 };
 
-// barrier indices
-enum { B_KV_FULL = 0, B_KV_EMPTY = 3, B_S_FULL = 6, B_S_EMPTY = 8, B_P_FULL = 10, B_O_FULL = 11, B_Q_FULL = 12,
-       B_Q_EMPTY = 13 };
+enum {
+  B_KFULL = 0, B_KEMPTY = 3, B_VFULL = 6, B_VEMPTY = 9, B_SFULL = 12, B_SEMPTY = 14, B_PFULL = 16, B_OFULL = 17,
+  B_QFULL = 18, B_QEMPTY = 20, B_INFO = 22   // B_INFO + kInfoRing <= 32
+};
 
 struct SeqShape {
   int n;   // query rows
@@ -93,13 +105,12 @@ __device__ void build_prefix(const DecodeParams& p, int* prefix, int* warp_tot, 
     int x = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      const int y = __shfl_up_sync(kFull, x, o);
       if (lane >= o) x += y;
     }
     if (lane == 31) warp_tot[warp] = x;
     __syncthreads();
-    int before = running;
-    int chunk = 0;
+    int before = running, chunk = 0;
     for (int w = 0; w < nwarps; ++w) {
       if (w < warp) before += warp_tot[w];
       chunk += warp_tot[w];
@@ -135,34 +146,84 @@ __device__ __forceinline__ Loc locate(int t, const int* prefix, int B, int KVH) 
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
   return v;
 }
-__device__ __forceinline__ float warp_sum(float v) {
+
+// Transposed butterfly over the 32 lanes of a warp for NR (power of two <= 32) columns held by every lane: each
+// stage sends half of the remaining columns to the partner lane and keeps the other half, so the whole reduction
+// costs NR - 1 + (5 - log2 NR) shuffles with the shuffles of a stage independent of each other.  On return lane l
+// holds the reduction of column l / (32 / NR) in v[0]; lanes with l % (32 / NR) == 0 store it to dst[column].
+template <int N, int O, bool kMax>
+__device__ __forceinline__ void column_stage(float* v, int lane) {
+  if constexpr (O > 0) {
+    if constexpr (N > 1) {
+      constexpr int H = N / 2;
+      const bool upper = (lane & O) != 0;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
+      for (int i = 0; i < H; ++i) {
+        const float send = upper ? v[i] : v[i + H];
+        const float keep = upper ? v[i + H] : v[i];
+        const float recv = __shfl_xor_sync(kFull, send, O);
+        v[i] = kMax ? fmaxf(keep, recv) : keep + recv;
+      }
+      column_stage<H, O / 2, kMax>(v, lane);
+    } else {
+      const float recv = __shfl_xor_sync(kFull, v[0], O);
+      v[0] = kMax ? fmaxf(v[0], recv) : v[0] + recv;
+      column_stage<1, O / 2, kMax>(v, lane);
+    }
+  }
+}
+
+template <int NR, bool kMax>
+__device__ __forceinline__ void column_reduce(float* v, float* dst, int lane) {
+  column_stage<NR, 16, kMax>(v, lane);
+  constexpr int kRep = 32 / NR;
+  if ((lane & (kRep - 1)) == 0) dst[lane / kRep] = v[0];
+}
+
+// Column reduction of NP (16, 32 or 48) values per thread within one warp into dst[0..NP).
+template <int NP, bool kMax>
+__device__ __forceinline__ void warp_columns(const float* x, float* dst, int lane) {
+  float v[32];
+  if constexpr (NP == 16) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = x[i];
+    column_reduce<16, kMax>(v, dst, lane);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = x[i];
+    column_reduce<32, kMax>(v, dst, lane);
+    if constexpr (NP == 48) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = x[32 + i];
+      column_reduce<16, kMax>(v, dst + 32, lane);
+    }
+  }
+}
+
+__device__ __forceinline__ bool all_ready(uint64_t* bar, uint32_t parity) {
+  return __all_sync(kFull, mbar_test_wait(bar, parity));
 }
 
 template <int NP>
 __global__ void __launch_bounds__(kThreads, 1)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const DecodeParams p) {
-  using L = Smem<NP>;
+  using C = Cfg<NP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBars);
-  int4* info = reinterpret_cast<int4*>(smem + L::kInfo);
-  float* red = reinterpret_cast<float*>(smem + L::kRed);
-  float* m_s = reinterpret_cast<float*>(smem + L::kM);
-  float* alpha_s = reinterpret_cast<float*>(smem + L::kAlpha);
-  float* lred = reinterpret_cast<float*>(smem + L::kLred);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmem);
-  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kAbort);
-  int* warp_tot = reinterpret_cast<int*>(smem + L::kScan);
-  int* prefix = reinterpret_cast<int*>(smem + L::kPrefix);
-  uint8_t* q_smem = smem + L::kQ;
-  uint8_t* p_smem = smem + L::kP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBars);
+  int4* info = reinterpret_cast<int4*>(smem + C::kInfo);       // [kInfoRing][2]
+  float* red = reinterpret_cast<float*>(smem + C::kRed);
+  float* m_s = reinterpret_cast<float*>(smem + C::kM);
+  float* alpha_s = reinterpret_cast<float*>(smem + C::kAlpha);
+  float* lred = reinterpret_cast<float*>(smem + C::kLred);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmem);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + C::kAbort);
+  int* warp_tot = reinterpret_cast<int*>(smem + C::kScan);
+  int* prefix = reinterpret_cast<int*>(smem + C::kPrefix);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -172,17 +233,20 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars[B_KV_FULL + s], 1);
-      mbar_init(&bars[B_KV_EMPTY + s], 1);
+      mbar_init(&bars[B_KFULL + s], 1);
+      mbar_init(&bars[B_KEMPTY + s], 1);
+      mbar_init(&bars[B_VFULL + s], 1);
+      mbar_init(&bars[B_VEMPTY + s], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[B_S_FULL + i], 1);
-      mbar_init(&bars[B_S_EMPTY + i], 128);
+      mbar_init(&bars[B_SFULL + i], 1);
+      mbar_init(&bars[B_SEMPTY + i], 128);
+      mbar_init(&bars[B_QFULL + i], 32);
+      mbar_init(&bars[B_QEMPTY + i], 1);
     }
-    mbar_init(&bars[B_P_FULL], 128);
-    mbar_init(&bars[B_O_FULL], 1);
-    mbar_init(&bars[B_Q_FULL], 32);
-    mbar_init(&bars[B_Q_EMPTY], 1);
+    mbar_init(&bars[B_PFULL], 128);
+    mbar_init(&bars[B_OFULL], 1);
+    for (int i = 0; i < kInfoRing; ++i) mbar_init(&bars[B_INFO + i], 1);
     *abort = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -203,108 +267,168 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   const int t_end = min(total, t_begin + per);
   const int ntiles = t_end > t_begin ? t_end - t_begin : 0;
 
-  if (warp == 0 && ntiles > 0) {
-    // ------------------------------------------------------------ TMA producer (whole warp waits, lane 0 issues)
-    for (int jj = 0; jj < ntiles; ++jj) {
-      const int t = t_begin + jj;
-      const int stage = jj % kStages;
-      if (!mbar_wait_warp(&bars[B_KV_EMPTY + stage], ((jj / kStages) & 1) ^ 1, abort)) break;
-      if (lane == 0) {
+  if ((warp == 0 || warp == 3) && ntiles > 0) {
+    // ------------------------------------------------------------ K (warp 0) and V (warp 3) producers
+    const bool is_k = warp == 0;
+    const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
+    uint8_t* ring = smem + (is_k ? C::kK : C::kV);
+    uint64_t* full = bars + (is_k ? B_KFULL : B_VFULL);
+    uint64_t* empty = bars + (is_k ? B_KEMPTY : B_VEMPTY);
+    bool stop = false;
+    for (int base = 0; base < ntiles && !stop; base += 32) {
+      // lane-parallel descriptors of the next 32 tiles (the block-table reads overlap each other)
+      int g = 0, j = 0, b = 0, row0 = 0, flags = 0, n = 0, L = 0, q0 = 0, nt = 0;
+      if (base + lane < ntiles) {
+        const int t = t_begin + base + lane;
         const Loc lc = locate(t, prefix, p.num_seqs, KVH);
-        const int tok0 = lc.j * kTileTokens;
-        int page = __ldg(p.block_tables + (int64_t)lc.b * p.bt_stride + tok0 / p.block_size);
+        b = lc.b;
+        g = lc.g;
+        j = lc.j;
+        nt = lc.nt;
+        const int tok0 = j * kTileTokens;
+        int page = __ldg(p.block_tables + (int64_t)b * p.bt_stride + tok0 / p.block_size);
         if (page < 0 || page >= p.num_blocks) {
-          atomicOr(&g_error_word, kErrBlockRange);
+          if (is_k) atomicOr(&g_error_word, kErrBlockRange);
           page = -1;   // TMA fills out-of-range rows with zeros; nothing outside the pool is read
         }
-        const int row0 = page * p.block_size + (tok0 % p.block_size);
-        const int flags = (lc.j == 0 || t == t_begin ? 1 : 0) | (lc.j == lc.nt - 1 || t == t_end - 1 ? 2 : 0);
-        info[stage] = make_int4(lc.b, lc.g, lc.j, flags);
-        uint64_t* full = &bars[B_KV_FULL + stage];
-        mbar_arrive_expect_tx(full, kStageBytes);
-        uint8_t* dst = smem + stage * kStageBytes;
-        tma_load_3d(dst, &tm_k, 0, lc.g, row0, full);
-        tma_load_3d(dst + kSlab, &tm_k, 64, lc.g, row0, full);
-        tma_load_3d(dst + 2 * kSlab, &tm_v, 0, lc.g, row0, full);
-        tma_load_3d(dst + 3 * kSlab, &tm_v, 64, lc.g, row0, full);
+        row0 = page * p.block_size + (tok0 % p.block_size);
+        flags = (j == 0 || t == t_begin ? 1 : 0) | (j == nt - 1 || t == t_end - 1 ? 2 : 0);
+        if (is_k) {
+          const SeqShape ss = seq_shape(p, b);
+          n = ss.n;
+          L = ss.L;
+          q0 = ss.q0;
+        }
       }
-      __syncwarp();
+      const int cnt = min(32, ntiles - base);
+      for (int i = 0; i < cnt; ++i) {
+        const int jj = base + i;
+        const int st = jj % kStages;
+        const int gi = __shfl_sync(kFull, g, i), ri = __shfl_sync(kFull, row0, i);
+        const int bi = __shfl_sync(kFull, b, i), ji = __shfl_sync(kFull, j, i), fi = __shfl_sync(kFull, flags, i);
+        const int ni = __shfl_sync(kFull, n, i), Li = __shfl_sync(kFull, L, i), qi = __shfl_sync(kFull, q0, i);
+        const int nti = __shfl_sync(kFull, nt, i);
+        if (!mbar_wait_warp(&empty[st], ((jj / kStages) & 1) ^ 1, abort)) {
+          stop = true;
+          break;
+        }
+        if (lane == 0) {
+          if (is_k) {
+            const int e = jj % kInfoRing;
+            info[2 * e] = make_int4(bi, gi, ji, fi);
+            info[2 * e + 1] = make_int4(ni, Li, qi, nti);
+            mbar_arrive(&bars[B_INFO + e]);
+          }
+          mbar_arrive_expect_tx(&full[st], kTileBytes);
+          uint8_t* dst = ring + st * kTileBytes;
+          tma_load_3d(dst, tm, 0, gi, ri, &full[st]);
+          tma_load_3d(dst + kSlab, tm, 64, gi, ri, &full[st]);
+        }
+        __syncwarp();
+      }
     }
   } else if (warp == 1 && ntiles > 0) {
-    // ------------------------------------------------------------ UMMA issuer (whole warp waits, lane 0 issues)
+    // ------------------------------------------------------------ UMMA issuer (whole warp polls, lane 0 issues)
     constexpr uint32_t idesc_qk = umma_idesc_bf16(128, NP, false, false);
-    constexpr uint32_t idesc_pv = umma_idesc_bf16(128, NP, true, false);
-    const uint32_t q_base = smem_u32(q_smem);
-    const uint32_t p_base = smem_u32(p_smem);
-    const uint32_t kv_base = smem_u32(smem);
-    int qi = 0;
-    auto issue_pv = [&](int ii) -> bool {
-      const int st = ii % kStages;
-      if (!mbar_wait_warp(&bars[B_P_FULL], ii & 1, abort)) return false;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t v_lo = kv_base + st * kStageBytes + 2 * kSlab;
+    constexpr uint32_t idesc_pv = umma_idesc_bf16(128, NP, true, true);
+    const uint32_t q_base = smem_u32(smem + C::kQ);
+    const uint32_t p_base = smem_u32(smem + C::kP);
+    const uint32_t k_base = smem_u32(smem + C::kK);
+    const uint32_t v_base = smem_u32(smem + C::kV);
+    int qk = 0, pv = 0, qseg = 0;
+    uint64_t last_progress = globaltimer();
+    while (pv < ntiles) {
+      bool did = false;
+      if (qk < ntiles) {
+        const int st = qk % kStages;
+        if (all_ready(&bars[B_KFULL + st], (qk / kStages) & 1)) {
+          const int flags = info[2 * (qk % kInfoRing)].w;
+          const int qb = qseg % C::kQBuf;
+          const bool q_ok = !(flags & 1) || all_ready(&bars[B_QFULL + qb], (qseg / C::kQBuf) & 1);
+          const int buf = qk & 1;
+          if (q_ok && all_ready(&bars[B_SEMPTY + buf], ((qk >> 1) & 1) ^ 1)) {
+            tc_fence_after();
+            if (lane == 0) {
+              const uint32_t kb = k_base + st * kTileBytes;
+              const uint32_t qbuf = q_base + qb * NP * 256;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint64_t a = umma_desc_sw128(v_lo + k * 2048, kSlab, 1024);
-          const uint64_t b = umma_desc_sw128(p_base + (k >> 2) * (NP * 128) + (k & 3) * 32, 16, 1024);
-          umma_bf16_ss(tmem + 2 * NP, a, b, idesc_pv, k > 0);
+              for (int k = 0; k < 8; ++k) {
+                const uint64_t a = umma_desc_sw128(kb + (k >> 2) * kSlab + (k & 3) * 32, 16, 1024);
+                const uint64_t bq = umma_desc_sw128(qbuf + (k >> 2) * (NP * 128) + (k & 3) * 32, 16, 1024);
+                umma_bf16_ss(tmem + buf * NP, a, bq, idesc_qk, k > 0);
+              }
+              umma_commit(&bars[B_SFULL + buf]);
+              umma_commit(&bars[B_KEMPTY + st]);
+              if (flags & 2) umma_commit(&bars[B_QEMPTY + qb]);
+            }
+            __syncwarp();
+            if (flags & 2) ++qseg;
+            ++qk;
+            did = true;
+          }
         }
-        umma_commit(&bars[B_O_FULL]);
-        umma_commit(&bars[B_KV_EMPTY + st]);
       }
-      __syncwarp();
-      return true;
-    };
-    bool ok = true;
-    for (int jj = 0; jj < ntiles && ok; ++jj) {
-      const int st = jj % kStages;
-      if (!mbar_wait_warp(&bars[B_KV_FULL + st], (jj / kStages) & 1, abort)) { ok = false; break; }
-      const int4 inf = info[st];
-      if (inf.w & 1) {
-        if (!mbar_wait_warp(&bars[B_Q_FULL], qi & 1, abort)) { ok = false; break; }
-      }
-      const int buf = jj & 1;
-      if (!mbar_wait_warp(&bars[B_S_EMPTY + buf], ((jj >> 1) & 1) ^ 1, abort)) { ok = false; break; }
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t k_lo = kv_base + st * kStageBytes;
+      if (pv < qk) {
+        const int st = pv % kStages;
+        if (all_ready(&bars[B_PFULL], pv & 1) && all_ready(&bars[B_VFULL + st], (pv / kStages) & 1)) {
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t vb = v_base + st * kTileBytes;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint64_t a = umma_desc_sw128(k_lo + (k >> 2) * kSlab + (k & 3) * 32, 16, 1024);
-          const uint64_t b = umma_desc_sw128(q_base + (k >> 2) * (NP * 128) + (k & 3) * 32, 16, 1024);
-          umma_bf16_ss(tmem + buf * NP, a, b, idesc_qk, k > 0);
+            for (int k = 0; k < 8; ++k) {
+              // A = V^T: 16 tokens (two 8-row groups, SBO 1024) x 128 dims (two 64-dim slabs, LBO 16 KB)
+              const uint64_t a = umma_desc_sw128(vb + k * 2048, kSlab, 1024);
+              // B = P^T: 16 tokens (two 8-token core-matrix groups, LBO 128) x NP rows (8-row groups, SBO 2048)
+              const uint64_t bp = umma_desc_noswz(p_base + k * 256, 128, 2048);
+              umma_bf16_ss(tmem + 2 * NP, a, bp, idesc_pv, k > 0);
+            }
+            umma_commit(&bars[B_OFULL]);
+            umma_commit(&bars[B_VEMPTY + st]);
+          }
+          __syncwarp();
+          ++pv;
+          did = true;
         }
-        umma_commit(&bars[B_S_FULL + buf]);
-        if (inf.w & 2) umma_commit(&bars[B_Q_EMPTY]);
       }
-      __syncwarp();
-      if (inf.w & 2) ++qi;
-      if (jj > 0) ok = issue_pv(jj - 1);
+      if (did) {
+        last_progress = globaltimer();
+      } else {
+        // warp-uniform decision to give up (the abort flag may be raised by another warp at any time)
+        const bool timed_out = globaltimer() - last_progress > kWaitLimitNs;
+        if (__any_sync(kFull, *abort != 0 || timed_out)) {
+          if (lane == 0 && *abort == 0) {
+            *abort = 1;
+            atomicOr(&g_error_word, kErrTimeout);
+          }
+          __syncwarp();
+          break;
+        }
+        sleep_ns(32);
+      }
     }
-    if (ok) issue_pv(ntiles - 1);
   } else if (warp == 2 && ntiles > 0) {
     // ------------------------------------------------------------ Q loader
     int qi = 0;
     int t = t_begin;
     while (t < t_end) {
       const Loc lc = locate(t, prefix, p.num_seqs, KVH);
-      if (!mbar_wait_warp(&bars[B_Q_EMPTY], (qi & 1) ^ 1, abort)) break;
+      const int qb = qi % C::kQBuf;
+      if (!mbar_wait_warp(&bars[B_QEMPTY + qb], ((qi / C::kQBuf) & 1) ^ 1, abort)) break;
       const SeqShape ss = seq_shape(p, lc.b);
       const int R = ss.n * G;
+      uint8_t* qs = smem + C::kQ + qb * NP * 256;
       for (int idx = lane; idx < NP * 16; idx += 32) {
         const int r = idx >> 4, c = idx & 15;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (r < R) {
-          const int i = r / G, h = r - i * G;
-          const __nv_bfloat16* src = p.q + (int64_t)(ss.q0 + i) * p.q_row_stride + (int64_t)(lc.g * G + h) * kHeadDim + c * 8;
-          v = __ldg(reinterpret_cast<const uint4*>(src));
-        }
-        *reinterpret_cast<uint4*>(q_smem + (c >> 3) * (NP * 128) + sw128_offset(r, c & 7)) = v;
+        const int rr = r < R ? r : 0;
+        const int i = rr / G, h = rr - i * G;
+        const __nv_bfloat16* src =
+            p.q + (int64_t)(ss.q0 + i) * p.q_row_stride + (int64_t)(lc.g * G + h) * kHeadDim + c * 8;
+        cp_async_16(qs + (c >> 3) * (NP * 128) + sw128_offset(r, c & 7), src, r < R ? 16u : 0u);
       }
+      cp_async_wait_all();
       fence_proxy_async_smem();
       __syncwarp();
-      mbar_arrive(&bars[B_Q_FULL]);
+      mbar_arrive(&bars[B_QFULL + qb]);
       ++qi;
       t = lc.s0 + lc.nt;   // next segment
     }
@@ -315,83 +439,90 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     const int ct = tid - kConsumerBase;       // TMEM lane: token ct of S^T, dim ct of O^T
     const int wq = ct >> 5;                   // lane quadrant
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+    const float inv_g = 1.0f / static_cast<float>(G);
+    uint8_t* p_smem = smem + C::kP;
     float l[NP], o[NP], s[NP];
-    SeqShape ss{0, 0, 0};
-    int R = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0;
+    int R = 0, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0;
     bool alive = true;
     for (int jj = 0; jj < ntiles; ++jj) {
       const int st = jj % kStages;
       const int buf = jj & 1;
-      const int rb = jj & 1;
-      alive = alive && mbar_wait_warp(&bars[B_KV_FULL + st], (jj / kStages) & 1, abort);
+      const int e = jj % kInfoRing;
+      alive = alive && mbar_wait_warp(&bars[B_INFO + e], (jj / kInfoRing) & 1, abort);
       int4 inf = make_int4(0, 0, 0, 0);
-      if (alive) inf = info[st];
+      if (alive) inf = info[2 * e];
       const bool first = inf.w & 1, last = inf.w & 2;
       if (alive && first) {
+        const int4 sh = info[2 * e + 1];
+        n = sh.x;
+        L = sh.y;
+        q0 = sh.z;
         seg_g = inf.y;
-        ss = seq_shape(p, inf.x);
-        R = ss.n * G;
-        const int nt = (ss.L + kTileTokens - 1) / kTileTokens;
-        seg_s0 = KVH * prefix[inf.x] + seg_g * nt;
-        seg_s1 = seg_s0 + nt;
+        R = n * G;
+        seg_s0 = KVH * prefix[inf.x] + seg_g * sh.w;
+        seg_s1 = seg_s0 + sh.w;
 #pragma unroll
-        for (int r = 0; r < NP; ++r) { l[r] = 0.f; o[r] = 0.f; }
+        for (int r = 0; r < NP; ++r) {
+          l[r] = 0.f;
+          o[r] = 0.f;
+        }
       }
       const int tok0 = inf.z * kTileTokens;
       const int tok = tok0 + ct;
-      // rows past the sequence end may hold stale or uninitialised values: zero V there so P = 0 cannot
-      // meet a NaN in the PV product
-      if (alive && ss.L - tok0 < kTileTokens && tok >= ss.L) {
-        uint8_t* vrow = smem + st * kStageBytes + 2 * kSlab + ct * 128;
+      // rows past the sequence end may hold stale or uninitialised values: zero V there so P = 0 cannot meet
+      // a NaN in the PV product (only the last tile of a sequence)
+      if (alive && L - tok0 < kTileTokens) {
+        alive = mbar_wait_warp(&bars[B_VFULL + st], (jj / kStages) & 1, abort);
+        if (alive && tok >= L) {
+          uint8_t* vrow = smem + C::kV + st * kTileBytes + ct * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-          *reinterpret_cast<uint4*>(vrow + kSlab + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+          for (int c = 0; c < 8; ++c) {
+            *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(vrow + kSlab + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+          }
         }
       }
       // ---- S tile -> masked, scaled scores; per-warp column maxima
-      alive = alive && mbar_wait_warp(&bars[B_S_FULL + buf], (jj >> 1) & 1, abort);
+      alive = alive && mbar_wait_warp(&bars[B_SFULL + buf], (jj >> 1) & 1, abort);
       if (alive) {
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < NP; c += 16) tmem_ld16(t_lane + buf * NP + c, s + c);
         tc_fence_before();
-        mbar_arrive(&bars[B_S_EMPTY + buf]);
-        const int lim = ss.L - ss.n;   // query i sees tokens <= lim + i
+        mbar_arrive(&bars[B_SEMPTY + buf]);
+        const int lim = L - n;   // query i sees tokens <= lim + i
 #pragma unroll
         for (int r = 0; r < NP; ++r) {
-          const bool vis = r < R && tok <= lim + r / G;
+          const int qrow = __float2int_rz((static_cast<float>(r) + 0.5f) * inv_g);
+          const bool vis = r < R && tok <= lim + qrow;
           s[r] = vis ? s[r] * p.scale_log2 : kNegInf;
-          if (r < R) {
-            const float mx = warp_max(s[r]);
-            if (lane == 0) red[(rb * 4 + wq) * NP + r] = mx;
-          }
         }
+        warp_columns<NP, true>(s, red + (buf * 4 + wq) * NP, lane);
       }
       if (named_bar_any(1, 128, !alive)) break;
-      // ---- running max (owner thread per row) and rescale factor
-      if (ct < R) {
-        const float* rr = red + rb * 4 * NP;
-        const float tm = fmaxf(fmaxf(rr[ct], rr[NP + ct]), fmaxf(rr[2 * NP + ct], rr[3 * NP + ct]));
-        const float mo = first ? kNegInf : m_s[ct];
-        const float mn = fmaxf(mo, tm);
+      // ---- running max (one owner thread per row) and rescale factor
+      if (ct < NP) {
+        float mn = 0.f, alpha = 1.f;
+        if (ct < R) {
+          const float* rr = red + buf * 4 * NP;
+          const float tm = fmaxf(fmaxf(rr[ct], rr[NP + ct]), fmaxf(rr[2 * NP + ct], rr[3 * NP + ct]));
+          const float mo = first ? kNegInf : m_s[ct];
+          mn = fmaxf(mo, tm);
+          alpha = (mn == kNegInf) ? 1.f : fast_exp2(mo - mn);
+        }
         m_s[ct] = mn;
-        alpha_s[rb * NP + ct] = (mn == kNegInf) ? 1.f : fast_exp2(mo - mn);
+        alpha_s[buf * NP + ct] = alpha;
       }
       named_bar_sync(1, 128);
 #pragma unroll
       for (int r = 0; r < NP; ++r) {
-        if (r < R) {
-          const float pr = (s[r] == kNegInf) ? 0.f : fast_exp2(s[r] - m_s[r]);
-          l[r] = l[r] * alpha_s[rb * NP + r] + pr;
-          s[r] = pr;
-        } else {
-          s[r] = 0.f;
-        }
+        const float pr = (s[r] == kNegInf) ? 0.f : fast_exp2(s[r] - m_s[r]);
+        l[r] = l[r] * alpha_s[buf * NP + r] + pr;
+        s[r] = pr;
       }
-      // ---- fold the previous tile's O; PV of tile jj-1 must be done before P is overwritten
+      // ---- fold the previous tile's O; PV of tile jj-1 must also be done before P is overwritten
       if (!first) {
-        alive = mbar_wait_warp(&bars[B_O_FULL], (jj - 1) & 1, abort);
+        alive = mbar_wait_warp(&bars[B_OFULL], (jj - 1) & 1, abort);
         if (alive) {
           tc_fence_after();
           float ot[16];
@@ -399,23 +530,28 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           for (int c = 0; c < NP; c += 16) {
             tmem_ld16(t_lane + 2 * NP + c, ot);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * alpha_s[(rb ^ 1) * NP + c + i] + ot[i];
+            for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * alpha_s[(buf ^ 1) * NP + c + i] + ot[i];
           }
           tc_fence_before();
         }
       }
-      // ---- P^T (bf16) into the K-major 128B-swizzled B operand: row r, token ct
+      // ---- P^T (bf16), MN-major without swizzle: 8 consecutive rows of token ct form one 16-byte vector
       if (alive) {
-        uint8_t* pb = p_smem + (ct >> 6) * (NP * 128);
-        const uint32_t chunk = (ct & 63) >> 3, sub = (ct & 7) * 2;
+        uint8_t* pb = p_smem + ct * 16;
 #pragma unroll
-        for (int r = 0; r < NP; ++r)
-          *reinterpret_cast<__nv_bfloat16*>(pb + sw128_offset(r, chunk) + sub) = __float2bfloat16_rn(s[r]);
+        for (int m = 0; m < NP / 8; ++m) {
+          uint4 v;
+          v.x = pack_bf16x2(s[8 * m + 0], s[8 * m + 1]);
+          v.y = pack_bf16x2(s[8 * m + 2], s[8 * m + 3]);
+          v.z = pack_bf16x2(s[8 * m + 4], s[8 * m + 5]);
+          v.w = pack_bf16x2(s[8 * m + 6], s[8 * m + 7]);
+          *reinterpret_cast<uint4*>(pb + m * 2048) = v;
+        }
         fence_proxy_async_smem();
-        mbar_arrive(&bars[B_P_FULL]);
+        mbar_arrive(&bars[B_PFULL]);
       }
       if (last && alive) {
-        alive = mbar_wait_warp(&bars[B_O_FULL], jj & 1, abort);
+        alive = mbar_wait_warp(&bars[B_OFULL], jj & 1, abort);
         if (alive) {
           tc_fence_after();
           float ot[16];
@@ -423,16 +559,10 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           for (int c = 0; c < NP; c += 16) {
             tmem_ld16(t_lane + 2 * NP + c, ot);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * alpha_s[rb * NP + c + i] + ot[i];
+            for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * alpha_s[buf * NP + c + i] + ot[i];
           }
           tc_fence_before();
-#pragma unroll
-          for (int r = 0; r < NP; ++r) {
-            if (r < R) {
-              const float sm = warp_sum(l[r]);
-              if (lane == 0) lred[wq * NP + r] = sm;
-            }
-          }
+          warp_columns<NP, false>(l, lred + wq * NP, lane);
         }
       }
       if (named_bar_any(1, 128, !alive)) break;
@@ -445,8 +575,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
             const float lt = lred[r] + lred[NP + r] + lred[2 * NP + r] + lred[3 * NP + r];
             const float val = lt > 0.f ? o[r] / lt : 0.f;
             if (complete) {
-              const int i = r / G, h = r - i * G;
-              p.out[(int64_t)(ss.q0 + i) * p.out_row_stride + (int64_t)(seg_g * G + h) * kHeadDim + ct] =
+              const int i = __float2int_rz((static_cast<float>(r) + 0.5f) * inv_g), h = r - i * G;
+              p.out[(int64_t)(q0 + i) * p.out_row_stride + (int64_t)(seg_g * G + h) * kHeadDim + ct] =
                   __float2bfloat16_rn(val);
             } else {
               p.part_o[((int64_t)slot * NP + r) * kHeadDim + ct] = val;
@@ -471,22 +601,25 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   }
 }
 
-// Merge the pieces of segments cut by CTA boundaries, and zero the rows of sequences with no keys.
+// Merge the pieces of segments cut by CTA boundaries, and zero the rows of sequences with no keys.  One warp per
+// query row of the segment; lanes own 4 dims each and walk the pieces with independent loads.
 template <int NP>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
 paged_decode_combine(const DecodeParams p, int main_grid) {
   __shared__ int prefix[kMaxDecodeSeqs + 1];
-  __shared__ int warp_tot[4];
-  const int tid = threadIdx.x;
-  build_prefix(p, prefix, warp_tot, tid, 128);
+  __shared__ int warp_tot[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  build_prefix(p, prefix, warp_tot, tid, 256);
   const int KVH = p.num_kv_heads, G = p.group;
   // zero-length sequences (batch padding): their rows see no key, output 0
   for (int b = blockIdx.x; b < p.num_seqs; b += gridDim.x) {
     const SeqShape ss = seq_shape(p, b);
     if (ss.n >= 1 && ss.n <= p.max_n && ss.L < 1) {
-      for (int i = 0; i < ss.n; ++i)
-        for (int h = 0; h < p.num_heads; ++h)
-          p.out[(int64_t)(ss.q0 + i) * p.out_row_stride + (int64_t)h * kHeadDim + tid] = __float2bfloat16_rn(0.f);
+      const int per_row = p.num_heads * kHeadDim;
+      for (int idx = tid; idx < ss.n * per_row; idx += 256) {
+        const int i = idx / per_row, rem = idx - i * per_row;
+        p.out[(int64_t)(ss.q0 + i) * p.out_row_stride + rem] = __float2bfloat16_rn(0.f);
+      }
     }
   }
   const int total = KVH * prefix[p.num_seqs];
@@ -498,24 +631,39 @@ paged_decode_combine(const DecodeParams p, int main_grid) {
     const int s1 = lc.s0 + lc.nt;
     if (lc.s0 >= t || (s1 - 1) / per != c) continue;   // not a cut segment ending in CTA c
     const int c0 = lc.s0 / per;
+    const int pieces = c - c0 + 1;
     const SeqShape ss = seq_shape(p, lc.b);
     const int R = ss.n * G;
-    for (int r = 0; r < R; ++r) {
-      float mx = p.part_lse[(2 * c0 + 1) * NP + r];
-      for (int cc = c0 + 1; cc <= c; ++cc) mx = fmaxf(mx, p.part_lse[(2 * cc) * NP + r]);
-      float acc = 0.f, den = 0.f;
+    for (int r = warp; r < R; r += 8) {
+      float mx = kNegInf;
+      for (int pi = lane; pi < pieces; pi += 32) {
+        const int slot = pi == 0 ? 2 * c0 + 1 : 2 * (c0 + pi);
+        mx = fmaxf(mx, p.part_lse[slot * NP + r]);
+      }
+      mx = warp_max(mx);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float den = 0.f;
       if (mx != kNegInf) {
-        for (int cc = c0; cc <= c; ++cc) {
-          const int slot = cc == c0 ? 2 * c0 + 1 : 2 * cc;
+#pragma unroll 4
+        for (int pi = 0; pi < pieces; ++pi) {
+          const int slot = pi == 0 ? 2 * c0 + 1 : 2 * (c0 + pi);
           const float lse = p.part_lse[slot * NP + r];
+          const float4 v = *reinterpret_cast<const float4*>(p.part_o + ((int64_t)slot * NP + r) * kHeadDim + lane * 4);
           const float w = lse == kNegInf ? 0.f : fast_exp2(lse - mx);
-          acc += w * p.part_o[((int64_t)slot * NP + r) * kHeadDim + tid];
+          acc.x += w * v.x;
+          acc.y += w * v.y;
+          acc.z += w * v.z;
+          acc.w += w * v.w;
           den += w;
         }
       }
+      const float inv = den > 0.f ? 1.f / den : 0.f;
       const int i = r / G, h = r - i * G;
-      p.out[(int64_t)(ss.q0 + i) * p.out_row_stride + (int64_t)(lc.g * G + h) * kHeadDim + tid] =
-          __float2bfloat16_rn(den > 0.f ? acc / den : 0.f);
+      __nv_bfloat16* dst = p.out + (int64_t)(ss.q0 + i) * p.out_row_stride + (int64_t)(lc.g * G + h) * kHeadDim + lane * 4;
+      uint2 packed;
+      packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+      packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+      *reinterpret_cast<uint2*>(dst) = packed;
     }
   }
 }
@@ -523,14 +671,14 @@ paged_decode_combine(const DecodeParams p, int main_grid) {
 template <int NP>
 cudaError_t launch_np(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const DecodeParams& p, int grid,
                       cudaStream_t stream) {
-  constexpr int smem = Smem<NP>::kBytes;
+  constexpr int smem = Cfg<NP>::kBytes;
   static_assert(smem <= 232448, "shared memory budget");
   cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   paged_decode_kernel<NP><<<grid, kThreads, smem, stream>>>(tm_k, tm_v, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  paged_decode_combine<NP><<<grid, 128, 0, stream>>>(p, grid);
+  paged_decode_combine<NP><<<grid, 256, 0, stream>>>(p, grid);
   return cudaGetLastError();
 }
 

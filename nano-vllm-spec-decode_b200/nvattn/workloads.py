@@ -54,8 +54,13 @@ def _table(gen, num_blocks: int, lens: list[int], width: int | None = None, bloc
 
 def _fill_cache(gen, k_cache, v_cache, table, lens, std, block_size=BLOCK_SIZE):
     """Random K/V for every block a sequence uses (whole blocks, so the tail past the length holds finite
-    stale values, like a reused block)."""
+    stale values, like a reused block).  With a device generator the whole pool is filled on the device
+    (fast; used by the benchmark, whose numbers do not depend on the values)."""
     KVH, D = k_cache.shape[2], k_cache.shape[3]
+    if gen.device.type != "cpu":
+        k_cache.normal_(0.0, std, generator=gen)
+        v_cache.normal_(0.0, std, generator=gen)
+        return
     for b, L in enumerate(lens):
         n = (L + block_size - 1) // block_size
         if n == 0:
@@ -75,7 +80,8 @@ def _slots(table, starts, ends, block_size=BLOCK_SIZE):
 
 def paged_decode_batch(lens: list[int], q_per_seq: int = 1, num_heads: int = 32, num_kv_heads: int = 8,
                        head_dim: int = 128, num_blocks: int = 2048, std: float = 0.5, seed: int = 0,
-                       dtype=torch.bfloat16, device="cpu", width: int | None = None, pad_seqs: int = 0) -> PagedBatch:
+                       dtype=torch.bfloat16, device="cpu", width: int | None = None, pad_seqs: int = 0,
+                       device_fill: bool = False) -> PagedBatch:
     """Decode / verify step: every sequence brings q_per_seq query tokens whose KV is already in the cache
     at positions [len - q_per_seq, len) (prepare_decode, model_runner.py:319-362).  pad_seqs appends empty
     sequences (length 0, table -1, slot -1) like graph-bucket padding."""
@@ -84,7 +90,7 @@ def paged_decode_batch(lens: list[int], q_per_seq: int = 1, num_heads: int = 32,
     k_cache = torch.zeros(num_blocks, BLOCK_SIZE, num_kv_heads, head_dim, dtype=dtype, device=device)
     v_cache = torch.zeros_like(k_cache)
     table = _table(gen, num_blocks, lens, width)
-    _fill_cache(gen, k_cache, v_cache, table, lens, std)
+    _fill_cache(torch.Generator(device).manual_seed(seed) if device_fill else gen, k_cache, v_cache, table, lens, std)
     T = B * q_per_seq
     q = (torch.randn(T, num_heads, head_dim, generator=gen) * std).to(dtype)
     slots = _slots(table, [L - q_per_seq for L in lens], lens)
@@ -105,19 +111,21 @@ def paged_decode_batch(lens: list[int], q_per_seq: int = 1, num_heads: int = 32,
 
 
 def decode_config(seed: int = 0, device="cpu", B: int = 64, num_heads: int = 32, num_kv_heads: int = 8,
-                  num_blocks: int = 2048) -> PagedBatch:
+                  num_blocks: int = 2048, device_fill: bool = False) -> PagedBatch:
     """Qwen3-8B decode, B=64, context U[512, 4096], pool 2048 blocks, N(0,1)*0.5."""
     gen = torch.Generator().manual_seed(seed)
     lens = torch.randint(512, 4097, (B,), generator=gen).tolist()
-    return paged_decode_batch(lens, 1, num_heads, num_kv_heads, 128, num_blocks, 0.5, seed + 1, device=device)
+    return paged_decode_batch(lens, 1, num_heads, num_kv_heads, 128, num_blocks, 0.5, seed + 1, device=device,
+                              device_fill=device_fill)
 
 
 def verify_config(k: int, seed: int = 0, device="cpu", B: int = 32, num_heads: int = 32, num_kv_heads: int = 8,
-                  num_blocks: int = 2048) -> PagedBatch:
+                  num_blocks: int = 2048, device_fill: bool = False) -> PagedBatch:
     """BASELINE config 3 (attention part): B=32, context U[256, 2048], k+1 query tokens per sequence."""
     gen = torch.Generator().manual_seed(seed)
     lens = torch.randint(256, 2049, (B,), generator=gen).tolist()
-    return paged_decode_batch(lens, k + 1, num_heads, num_kv_heads, 128, num_blocks, 0.5, seed + 1, device=device)
+    return paged_decode_batch(lens, k + 1, num_heads, num_kv_heads, 128, num_blocks, 0.5, seed + 1, device=device,
+                              device_fill=device_fill)
 
 
 def accept_config(k: int, S: int = 32, p_match: float = 0.7, vocab: int = 151936, seed: int = 0):
