@@ -112,6 +112,29 @@ NVA_API int nva_greedy_accept(const void* target_ids, int64_t target_row_stride,
                               int32_t id_bytes, void* num_accepted, void* next_tokens, void* stream);
 
 /*
+ * Paged decode / verify attention without a caller workspace.  No counterpart in the reference: nano-vllm always
+ * lets flash-attn allocate.  Same arguments and results as nva_paged_decode, minus the workspace.
+ * It serves callers that cannot allocate device memory -- code running inside an allocator hook or a host callback
+ * (where a cudaMalloc would recurse or deadlock), runtimes that carve all memory out of an arena reserved at start-up,
+ * embedders whose memory manager has no device allocation -- by keeping the split-KV partials in a fixed array
+ * compiled into the library: NVA_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads the library until the
+ * process exits.  The call itself allocates nothing (no cudaMalloc / cudaFree, no allocating library routine).
+ *  - The first call on each device looks up the array's device address (cudaGetSymbolAddress, that device current)
+ *    and caches it: make that first call before any stream capture.
+ *  - A call needing more than NVA_NOALLOC_SCRATCH_BYTES (2 x SMs x rows x 129 x 4 bytes, rows = q_per_seq x
+ *    num_heads / num_kv_heads rounded up to 16, 32 or 48) returns NVA_ERR_WORKSPACE before launching anything; on a
+ *    148-SM B200 that admits up to 32 rows (decode, and verify with up to 7 drafts at 4 q heads per kv head).
+ *  - All calls on a device share the array and leave their contents in it; nothing in it needs clearing between
+ *    calls, but calls that overlap on the GPU (e.g. on two streams) race on it and must be serialised by the caller.
+ */
+#define NVA_NOALLOC_SCRATCH_BYTES (6u << 20)
+NVA_API int nva_paged_decode_noalloc(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
+                                     int32_t num_blocks, int32_t block_size, const int32_t* context_lens,
+                                     const int32_t* block_tables, int32_t bt_row_stride, int32_t num_seqs,
+                                     int32_t q_per_seq, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                                     float softmax_scale, void* out, int64_t out_row_stride, void* stream);
+
+/*
  * Device error word.  Kernels never trap: a slot or block id out of range, or a pipeline wait that ran past its
  * time limit, sets a bit here and the kernel skips the access or returns.  Reading it synchronises the device.
  * Bits: 1 = scatter slot out of range, 2 = pipeline wait timed out, 4 = block id out of range.

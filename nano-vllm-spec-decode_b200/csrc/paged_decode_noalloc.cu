@@ -1,0 +1,149 @@
+// nva_paged_decode_noalloc: the paged decode / verify attention of nva_paged_decode for callers that cannot
+// allocate device memory.
+//
+// nva_paged_decode needs a caller workspace for the split-KV partials.  Some callers have no way to provide one:
+// code that runs inside an allocator hook or a host callback (where a cudaMalloc would recurse or deadlock),
+// runtimes that carve every byte out of an arena reserved at start-up and only hand out the tensors they own, and
+// embedders whose memory manager exposes no device allocation at all.  For them the partials live here, in a
+// fixed array compiled into the library (NVA_NOALLOC_SCRATCH_BYTES on every GPU that loads it, held until the
+// process exits).  The kernels are the same ones nva_paged_decode launches; only the scratch pointer differs.
+//
+// Rules of use (also stated in include/nvattn.h):
+//  - the first call on each device looks up the array's device address with cudaGetSymbolAddress, with that device
+//    current, and caches it; make that first call before any stream capture;
+//  - every call on a device shares the one array and leaves its contents behind; nothing in it has to start at zero
+//    (each partial the combine step reads was written earlier in the same call), but calls that overlap on the GPU
+//    (two streams, say) race on it and must be serialised by the caller;
+//  - a call that needs more than NVA_NOALLOC_SCRATCH_BYTES is rejected with NVA_ERR_WORKSPACE before any launch;
+//  - nothing here allocates: no cudaMalloc, no cudaFree, no allocating library routine.
+#include <cudaTypedefs.h>
+#include <mutex>
+
+#include "../../include/nvattn.h"
+#include "nva_kernels.h"
+
+namespace {
+
+// The scratch.  Host code must not pass this symbol to a kernel: in host code it is only a stand-in, its device
+// address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NVA_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+int g_sm_count[kMaxDevices] = {};
+
+// Device address of the scratch and the SM count of the current device, looked up once per device.
+int current_device_scratch(void** addr, int* sms) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NVA_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return NVA_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return NVA_ERR_CUDA;
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      return NVA_ERR_CUDA;
+    g_sm_count[dev] = n;
+    g_scratch_addr[dev] = p;
+  }
+  *addr = g_scratch_addr[dev];
+  *sms = g_sm_count[dev];
+  return NVA_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// {128 dims, heads, rows} bf16 view of a KV cache, 64 x 1 x 128 boxes with 128-byte swizzle (the kernels' layout).
+bool cache_map(CUtensorMap* tm, const void* base, int64_t heads, int64_t rows) {
+  auto fn = tensor_map_encoder();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {128 * 2, static_cast<cuuint64_t>(heads * 128 * 2)};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" NVA_API int nva_paged_decode_noalloc(const void* q, int64_t q_row_stride, const void* k_cache,
+                                                const void* v_cache, int32_t num_blocks, int32_t block_size,
+                                                const int32_t* context_lens, const int32_t* block_tables,
+                                                int32_t bt_row_stride, int32_t num_seqs, int32_t q_per_seq,
+                                                int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                                                float softmax_scale, void* out, int64_t out_row_stride,
+                                                void* stream) {
+  // the same argument checks as nva_paged_decode
+  if (num_seqs < 0 || q_per_seq < 1 || num_heads <= 0 || num_kv_heads <= 0) return NVA_ERR_INVALID_ARGUMENT;
+  if (num_heads % num_kv_heads != 0) return NVA_ERR_INVALID_ARGUMENT;
+  if (head_dim != nva::kHeadDim) return NVA_ERR_UNSUPPORTED;
+  if (num_seqs == 0) return NVA_OK;
+  if (num_seqs > nva::kMaxDecodeSeqs) return NVA_ERR_UNSUPPORTED;
+  if (k_cache == nullptr || v_cache == nullptr || num_blocks <= 0 || block_size <= 0) return NVA_ERR_INVALID_ARGUMENT;
+  if (block_size % nva::kTileTokens != 0) return NVA_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(num_blocks) * block_size >= (int64_t(1) << 31)) return NVA_ERR_UNSUPPORTED;
+  if (q == nullptr || out == nullptr || context_lens == nullptr || block_tables == nullptr || bt_row_stride < 1)
+    return NVA_ERR_INVALID_ARGUMENT;
+  if (q_row_stride < static_cast<int64_t>(num_heads) * head_dim ||
+      out_row_stride < static_cast<int64_t>(num_heads) * head_dim)
+    return NVA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(q) || (q_row_stride % 8) != 0 || !aligned16(out) ||
+      (out_row_stride % 8) != 0)
+    return NVA_ERR_ALIGNMENT;
+  const int group = num_heads / num_kv_heads;
+  const int np = nva::decode_rows_padded(q_per_seq * group);
+  if (np == 0) return NVA_ERR_UNSUPPORTED;
+
+  void* scratch = nullptr;
+  int grid = 0;
+  int rc = current_device_scratch(&scratch, &grid);
+  if (rc != NVA_OK) return rc;
+  // the partials of one call: 2 pieces per CTA x np rows x (128 dims + log-sum-exp) floats
+  if (nva::decode_workspace_bytes(grid, np) > NVA_NOALLOC_SCRATCH_BYTES) return NVA_ERR_WORKSPACE;
+
+  CUtensorMap tm_k, tm_v;
+  const int64_t rows = static_cast<int64_t>(num_blocks) * block_size;
+  if (!cache_map(&tm_k, k_cache, num_kv_heads, rows) || !cache_map(&tm_v, v_cache, num_kv_heads, rows))
+    return NVA_ERR_CUDA;
+
+  nva::DecodeParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.q_row_stride = q_row_stride;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_row_stride = out_row_stride;
+  p.cu_q = nullptr;
+  p.cu_k = nullptr;
+  p.ctx_lens = context_lens;
+  p.block_tables = block_tables;
+  p.bt_stride = bt_row_stride;
+  p.num_seqs = num_seqs;
+  p.n_fixed = q_per_seq;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.group = group;
+  p.max_n = np / group;
+  p.block_size = block_size;
+  p.num_blocks = num_blocks;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.part_o = static_cast<float*>(scratch);
+  p.part_lse = p.part_o + static_cast<size_t>(2) * grid * np * nva::kHeadDim;
+  const cudaError_t e = nva::launch_paged_decode(tm_k, tm_v, p, np, grid, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? NVA_OK : NVA_ERR_CUDA;
+}
