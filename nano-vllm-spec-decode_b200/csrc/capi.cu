@@ -5,6 +5,7 @@
 #include <cudaTypedefs.h>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 
 #include "../../include/nvattn.h"
@@ -184,17 +185,25 @@ NVA_API int nva_paged_decode(const void* q, int64_t q_row_stride, const void* k_
   return e == cudaSuccess ? NVA_OK : cuda_fail(e);
 }
 
+}  // extern "C"
+
+namespace {
+
+// Varlen workspace: the decode kernel's split partials (48-row tiles) followed by the prefill work plan.
+size_t varlen_decode_part(int sms) { return (nva::decode_workspace_bytes(sms, 48) + 255) & ~size_t(255); }
+int varlen_plan_capacity(int32_t num_seqs, int32_t total_q) { return total_q / 128 + num_seqs + 1; }
+
+}  // namespace
+
+extern "C" {
+
 NVA_API size_t nva_varlen_workspace_bytes(int32_t num_seqs, int32_t total_q, int32_t num_heads,
                                           int32_t num_kv_heads, int32_t head_dim) {
-  (void)num_seqs;
-  (void)total_q;
   (void)head_dim;
-  if (num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return 0;
-  const int group = num_heads / num_kv_heads;
-  const int np = nva::decode_rows_padded(group);   // rows of a 1-token query (the widest of 16/32/48 that fits)
+  if (num_kv_heads <= 0 || num_heads % num_kv_heads != 0 || num_seqs < 0 || total_q < 0) return 0;
   const int sms = sm_count();
-  if (np == 0 || sms == 0) return 0;
-  return nva::decode_workspace_bytes(sms, 48);
+  if (sms == 0) return 0;
+  return varlen_decode_part(sms) + sizeof(int32_t) * (1 + static_cast<size_t>(varlen_plan_capacity(num_seqs, total_q)));
 }
 
 NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void* key, int64_t key_row_stride,
@@ -237,10 +246,12 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
   if (grid == 0) return cuda_fail(cudaGetLastError());
   const int np = 48;
   const int max_n = np / group;                // query runs up to this length use the decode kernel
+  const int cap = varlen_plan_capacity(num_seqs, total_q);
+  if (cap > nva::kMaxPrefillTiles) return NVA_ERR_UNSUPPORTED;
+  const size_t need = varlen_decode_part(grid) + sizeof(int32_t) * (1 + static_cast<size_t>(cap));
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return NVA_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (paged) {
-    const size_t need = nva::decode_workspace_bytes(grid, np);
-    if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return NVA_ERR_WORKSPACE;
     nva::DecodeParams p{};
     p.q = static_cast<const __nv_bfloat16*>(q);
     p.q_row_stride = q_row_stride;
@@ -284,9 +295,11 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
     pp.min_q = paged ? max_n + 1 : 1;
     pp.block_size = block_size;
     pp.num_blocks = num_blocks;
-    pp.q_tiles_bound = (total_q + 127) / 128 + num_seqs;
+    pp.q_tiles_bound = cap;
     pp.scale_log2 = softmax_scale * 1.4426950408889634f;
-    cudaError_t e = nva::launch_prefill(tm_q, tm_k, tm_v, pp, s);
+    pp.plan = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + varlen_decode_part(grid));
+    const int pgrid = static_cast<int>(std::min<int64_t>(grid, static_cast<int64_t>(cap) * num_heads));
+    cudaError_t e = nva::launch_prefill(tm_q, tm_k, tm_v, pp, pgrid, s);
     if (e != cudaSuccess) return cuda_fail(e);
   }
   return NVA_OK;

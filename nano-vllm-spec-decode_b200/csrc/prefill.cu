@@ -1,6 +1,471 @@
+// Varlen causal prefill attention for sm_100a (replaces flash_attn_varlen_func at nanovllm/layers/attention.py:67-70
+// for query runs longer than the decode kernel's 48-row tile: prefill chunks, with or without a paged prefix).
+//
+// Work item = (128-row query tile of one sequence, q head).  A one-CTA plan kernel lists the query tiles heaviest
+// first (most key tiles under the causal mask), and persistent CTAs take items round-robin from that list, so the
+// long diagonal tiles start first and the short ones fill the tail.
+//
+// Per item: S = Q K^T with M = 128 query rows on the TMEM lanes, N = 128 keys (A = Q, B = K tile, both K-major
+// 128B-swizzled straight from TMA); P = exp2(S * scale - m) in bf16 through 128B-swizzled shared memory; O += P V in
+// TMEM (A = P, K-major; B = V tile, MN-major, straight from TMA).  One thread owns one query row: its maximum and sum
+// are thread-local (no shuffles, no barriers between the softmax warps).  O is rescaled in TMEM only when a row's
+// maximum grows by more than 2^8 (until then P values up to 256 are exact enough in bf16 and FP32 sums).
+//
+// Warp roles (256 threads): 0 = Q + K producer (also publishes the item descriptors), 3 = V producer, 1 = TMEM owner
+// + UMMA issuer (polls, issues whichever product is ready), 2 = idle, 4..7 = softmax + epilogue.
+#include "nva_ptx.cuh"
 #include "nva_kernels.h"
+
 namespace nva {
-cudaError_t launch_prefill(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const PrefillParams&, cudaStream_t) {
-  return cudaErrorNotSupported;
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kSlab = 128 * 128;       // 128 rows x 128 bytes
+constexpr int kTile = 2 * kSlab;       // 128 rows x 256 bytes (all 128 dims, or 128 keys of P)
+constexpr int kItemRing = 8;           // item descriptors: producer is at most ~5 items ahead of the softmax warps
+constexpr float kNegInf = -__builtin_huge_valf();
+constexpr uint32_t kFull = 0xffffffffu;
+constexpr float kRescaleLog2 = 8.0f;   // rescale O only when a row maximum grows by more than this (log2 units)
+
+// shared memory map (offsets from a 1024-aligned base)
+constexpr int kOffQ = 0;                    // 2 x Q tile
+constexpr int kOffK = kOffQ + 2 * kTile;    // 2-stage K ring
+constexpr int kOffV = kOffK + 2 * kTile;    // 2-stage V ring
+constexpr int kOffP = kOffV + 2 * kTile;    // P tile
+constexpr int kOffBars = kOffP + kTile;     // 32 x u64
+constexpr int kOffItems = kOffBars + 32 * 8;      // kItemRing x 2 x int4
+constexpr int kOffTmem = kOffItems + kItemRing * 32;
+constexpr int kOffAbort = kOffTmem + 4;
+constexpr int kSmemBytes = kOffAbort + 4 + 1024;
+static_assert(kSmemBytes <= 232448, "prefill shared memory budget");
+
+enum {
+  B_QFULL = 0, B_QEMPTY = 2, B_KFULL = 4, B_KEMPTY = 6, B_VFULL = 8, B_VEMPTY = 10, B_SFULL = 12, B_SEMPTY = 14,
+  B_PFULL = 16, B_ODONE = 17, B_ITEM = 18   // B_ITEM + kItemRing <= 32
+};
+
+struct Item {
+  int b, qt, h, nkv;   // sequence, query tile, q head, key tiles under the causal mask
+  int n, L, q0, k0;    // query rows, keys, first query row, first key row (contiguous K/V only)
+  int rows;            // valid query rows in this tile
+  bool valid;
+};
+
+// Item k of a CTA's sequence: plan entry k / H, head k % H.
+__device__ __forceinline__ Item load_item(const PrefillParams& p, int k, int total) {
+  Item it;
+  const int pidx = k / p.num_heads;
+  it.valid = pidx < total;
+  if (!it.valid) return it;
+  const int e = p.plan[1 + pidx];
+  it.b = e >> 12;
+  it.qt = e & 0xfff;
+  it.h = k - pidx * p.num_heads;
+  it.q0 = __ldg(p.cu_q + it.b);
+  it.n = __ldg(p.cu_q + it.b + 1) - it.q0;
+  it.k0 = __ldg(p.cu_k + it.b);
+  it.L = __ldg(p.cu_k + it.b + 1) - it.k0;
+  it.rows = min(128, it.n - it.qt * 128);
+  const int last_row = it.qt * 128 + it.rows - 1;
+  // keys [0, L - n + last_row] are visible to the tile; at least one (fully masked) tile keeps the pipeline
+  // uniform when no key is visible (those rows get a zero output)
+  it.nkv = max(1, (it.L - it.n + last_row) / 128 + 1);
+  return it;
 }
+
+__device__ __forceinline__ bool all_ready(uint64_t* bar, uint32_t parity) {
+  return __all_sync(kFull, mbar_test_wait(bar, parity));
 }
+
+// ------------------------------------------------------------------------------------------------ plan kernel
+// plan[0] = number of query tiles of sequences with q_len >= min_q; plan[1 + i] = (seq << 12) | tile, ordered by
+// descending key-tile count (ties by position), so persistent CTAs start the longest items first.
+__global__ void __launch_bounds__(1024) prefill_plan_kernel(const PrefillParams p) {
+  __shared__ int cost[kMaxPrefillTiles];
+  __shared__ int code[kMaxPrefillTiles];
+  __shared__ int warp_tot[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // tiles per sequence and their exclusive prefix (B <= 1024: one element per thread)
+  int nt = 0, n = 0, L = 0;
+  if (tid < p.num_seqs) {
+    const int a = p.cu_q[tid];
+    n = p.cu_q[tid + 1] - a;
+    L = p.cu_k[tid + 1] - p.cu_k[tid];
+    nt = n >= p.min_q && n > 0 ? (n + 127) / 128 : 0;
+  }
+  int x = nt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(kFull, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  int before = 0, total = 0;
+  for (int w = 0; w < 32; ++w) {
+    if (w < warp) before += warp_tot[w];
+    total += warp_tot[w];
+  }
+  const int off = before + x - nt;
+  const int cap = min(p.q_tiles_bound, kMaxPrefillTiles);
+  total = min(total, cap);
+  for (int qt = 0; qt < nt; ++qt) {
+    const int i = off + qt;
+    if (i < cap) {
+      const int rows = min(128, n - qt * 128);
+      cost[i] = (L - n + qt * 128 + rows - 1) / 128 + 1;
+      code[i] = (tid << 12) | qt;
+    }
+  }
+  __syncthreads();
+  // rank by (cost desc, index asc); O(total^2 / 1024) comparisons
+  for (int i = tid; i < total; i += 1024) {
+    const int ci = cost[i];
+    int rank = 0;
+    for (int j = 0; j < total; ++j) {
+      const int cj = cost[j];
+      rank += (cj > ci) || (cj == ci && j < i);
+    }
+    p.plan[1 + rank] = code[i];
+  }
+  if (tid == 0) p.plan[0] = total;
+}
+
+// ------------------------------------------------------------------------------------------------ main kernel
+__global__ void __launch_bounds__(kThreads, 1)
+prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+               const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
+  int4* items = reinterpret_cast<int4*>(smem + kOffItems);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + kOffAbort);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool paged = p.block_tables != nullptr;
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[B_QFULL + i], 1);
+      mbar_init(&bars[B_QEMPTY + i], 1);
+      mbar_init(&bars[B_KFULL + i], 1);
+      mbar_init(&bars[B_KEMPTY + i], 1);
+      mbar_init(&bars[B_VFULL + i], 1);
+      mbar_init(&bars[B_VEMPTY + i], 1);
+      mbar_init(&bars[B_SFULL + i], 1);
+      mbar_init(&bars[B_SEMPTY + i], 128);
+    }
+    mbar_init(&bars[B_PFULL], 128);
+    mbar_init(&bars[B_ODONE], 1);
+    for (int i = 0; i < kItemRing; ++i) mbar_init(&bars[B_ITEM + i], 1);
+    *abort = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = p.plan[0];
+  const int n_items = total * p.num_heads;
+
+  if (warp == 0 || warp == 3) {
+    // ------------------------------------------------------------ Q+K (warp 0) and V (warp 3) producers
+    const bool is_k = warp == 0;
+    const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
+    uint8_t* ring = smem + (is_k ? kOffK : kOffV);
+    uint64_t* full = bars + (is_k ? B_KFULL : B_VFULL);
+    uint64_t* empty = bars + (is_k ? B_KEMPTY : B_VEMPTY);
+    int g = 0, it_count = 0;
+    bool stop = false;
+    for (int k = blockIdx.x; k < n_items && !stop; k += gridDim.x, ++it_count) {
+      const Item it = load_item(p, k, total);
+      const int kvh = it.h / p.group;
+      if (is_k) {
+        if (lane == 0) {
+          const int e = it_count % kItemRing;
+          items[2 * e] = make_int4(it.b, it.qt, it.h, it.nkv);
+          items[2 * e + 1] = make_int4(it.n, it.L, it.q0, it.rows);
+          mbar_arrive(&bars[B_ITEM + e]);
+        }
+        const int qb = it_count & 1;
+        if (!mbar_wait_warp(&bars[B_QEMPTY + qb], ((it_count >> 1) & 1) ^ 1, abort)) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bars[B_QFULL + qb], kTile);
+          uint8_t* dst = smem + kOffQ + qb * kTile;
+          tma_load_3d(dst, &tm_q, 0, it.h, it.q0 + it.qt * 128, &bars[B_QFULL + qb]);
+          tma_load_3d(dst + kSlab, &tm_q, 64, it.h, it.q0 + it.qt * 128, &bars[B_QFULL + qb]);
+        }
+        __syncwarp();
+      }
+      for (int base = 0; base < it.nkv && !stop; base += 32) {
+        // key-tile rows for the next 32 tiles (block-table reads in parallel across lanes)
+        int row0 = 0;
+        if (base + lane < it.nkv) {
+          const int tok0 = (base + lane) * 128;
+          if (paged) {
+            int page = __ldg(p.block_tables + (int64_t)it.b * p.bt_stride + tok0 / p.block_size);
+            if (page < 0 || page >= p.num_blocks) {
+              if (is_k) atomicOr(&g_error_word, kErrBlockRange);
+              page = -1;   // rows filled with zeros by TMA; nothing outside the pool is read
+            }
+            row0 = page * p.block_size + tok0 % p.block_size;
+          } else {
+            row0 = it.k0 + tok0;
+          }
+        }
+        const int cnt = min(32, it.nkv - base);
+        for (int i = 0; i < cnt; ++i, ++g) {
+          const int r0 = __shfl_sync(kFull, row0, i);
+          const int st = g & 1;
+          if (!mbar_wait_warp(&empty[st], ((g >> 1) & 1) ^ 1, abort)) {
+            stop = true;
+            break;
+          }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[st], kTile);
+            tma_load_3d(ring + st * kTile, tm, 0, kvh, r0, &full[st]);
+            tma_load_3d(ring + st * kTile + kSlab, tm, 64, kvh, r0, &full[st]);
+          }
+          __syncwarp();
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    constexpr uint32_t idesc_qk = umma_idesc_bf16(128, 128, false, false);
+    constexpr uint32_t idesc_pv = umma_idesc_bf16(128, 128, false, true);
+    const uint32_t q_base = smem_u32(smem + kOffQ), k_base = smem_u32(smem + kOffK);
+    const uint32_t v_base = smem_u32(smem + kOffV), p_base = smem_u32(smem + kOffP);
+    // QK cursor (item, tile) and PV cursor (item, tile); item lengths come from the descriptor ring
+    int it_q = 0, j_q = 0, nkv_q = -1, gq = 0;
+    int it_p = 0, j_p = 0, nkv_p = -1, gp = 0;
+    const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    uint64_t last_progress = globaltimer();
+    while (it_p < my_items) {
+      bool did = false;
+      if (it_q < my_items) {
+        const int e = it_q % kItemRing;
+        if (nkv_q < 0 && all_ready(&bars[B_ITEM + e], (it_q / kItemRing) & 1)) nkv_q = items[2 * e].w;
+        const int st = gq & 1, qb = it_q & 1;
+        if (nkv_q >= 0 && (j_q > 0 || all_ready(&bars[B_QFULL + qb], (it_q >> 1) & 1)) &&
+            all_ready(&bars[B_KFULL + st], (gq >> 1) & 1) && all_ready(&bars[B_SEMPTY + st], ((gq >> 1) & 1) ^ 1)) {
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t qa = q_base + qb * kTile, kb = k_base + st * kTile;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t a = umma_desc_sw128(qa + (kk >> 2) * kSlab + (kk & 3) * 32, 16, 1024);
+              const uint64_t b = umma_desc_sw128(kb + (kk >> 2) * kSlab + (kk & 3) * 32, 16, 1024);
+              umma_bf16_ss(tmem + st * 128, a, b, idesc_qk, kk > 0);
+            }
+            umma_commit(&bars[B_SFULL + st]);
+            umma_commit(&bars[B_KEMPTY + st]);
+            if (j_q == nkv_q - 1) umma_commit(&bars[B_QEMPTY + qb]);
+          }
+          __syncwarp();
+          ++gq;
+          if (++j_q == nkv_q) {
+            j_q = 0;
+            nkv_q = -1;
+            ++it_q;
+          }
+          did = true;
+        }
+      }
+      if (gp < gq) {
+        if (nkv_p < 0) nkv_p = items[2 * (it_p % kItemRing)].w;   // published before QK of this item ran
+        const int st = gp & 1;
+        if (all_ready(&bars[B_PFULL], gp & 1) && all_ready(&bars[B_VFULL + st], (gp >> 1) & 1)) {
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t vb = v_base + st * kTile;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t a = umma_desc_sw128(p_base + (kk >> 2) * kSlab + (kk & 3) * 32, 16, 1024);
+              const uint64_t b = umma_desc_sw128(vb + kk * 2048, kSlab, 1024);
+              umma_bf16_ss(tmem + 256, a, b, idesc_pv, (j_p > 0 || kk > 0) ? 1u : 0u);   // fresh O per item
+            }
+            umma_commit(&bars[B_ODONE]);
+            umma_commit(&bars[B_VEMPTY + st]);
+          }
+          __syncwarp();
+          ++gp;
+          if (++j_p == nkv_p) {
+            j_p = 0;
+            nkv_p = -1;
+            ++it_p;
+          }
+          did = true;
+        }
+      }
+      if (did) {
+        last_progress = globaltimer();
+      } else {
+        const bool timed_out = globaltimer() - last_progress > kWaitLimitNs;
+        if (__any_sync(kFull, *abort != 0 || timed_out)) {
+          if (lane == 0 && *abort == 0) {
+            *abort = 1;
+            atomicOr(&g_error_word, kErrTimeout);
+          }
+          __syncwarp();
+          break;
+        }
+        sleep_ns(32);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax + epilogue (thread = query row)
+    const int t = tid - 128;
+    const int wq = t >> 5;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+    int g = 0, pv_seen = 0, it_count = 0;
+    bool alive = true;
+    for (int k = blockIdx.x; k < n_items && alive; k += gridDim.x, ++it_count) {
+      const int e = it_count % kItemRing;
+      alive = mbar_wait_warp(&bars[B_ITEM + e], (it_count / kItemRing) & 1, abort);
+      if (!alive) break;
+      const int4 i0 = items[2 * e], i1 = items[2 * e + 1];
+      const int h = i0.z, nkv = i0.w, n = i1.x, L = i1.y, q0 = i1.z, rows = i1.w, qt = i0.y;
+      const int lim = L - n + qt * 128 + t;   // this row sees keys <= lim
+      float m_used = kNegInf, l = 0.f;
+      for (int j = 0; j < nkv && alive; ++j, ++g) {
+        const int st = g & 1;
+        // paged keys past the sequence end may be stale or uninitialised: zero V there (P is 0 there anyway)
+        if (paged && j * 128 + 127 >= L) {
+          alive = mbar_wait_warp(&bars[B_VFULL + st], (g >> 1) & 1, abort);
+          if (!alive) break;
+          if (j * 128 + t >= L) {
+            uint8_t* vrow = smem + kOffV + st * kTile + t * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+              *reinterpret_cast<uint4*>(vrow + kSlab + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
+          }
+        }
+        alive = mbar_wait_warp(&bars[B_SFULL + st], (g >> 1) & 1, abort);
+        if (!alive) break;
+        tc_fence_after();
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 128; c += 32) tmem_ld32(t_lane + st * 128 + c, s + c);
+        tc_fence_before();
+        mbar_arrive(&bars[B_SEMPTY + st]);
+        const int kmax = lim - j * 128;          // columns > kmax are masked for this row
+        float mx = kNegInf;
+        if (kmax >= 127) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) mx = fmaxf(mx, s[c]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) {
+            s[c] = c <= kmax ? s[c] : kNegInf;
+            mx = fmaxf(mx, s[c]);
+          }
+        }
+        const float m_cand = fmaxf(m_used, mx * p.scale_log2);
+        const bool rescale = m_used != kNegInf && m_cand > m_used + kRescaleLog2;
+        // P buffer reuse and any O rescale both need the previous PV product complete
+        if (pv_seen < g) {
+          alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
+          if (!alive) break;
+          pv_seen = g;
+        }
+        if (j > 0 && __any_sync(kFull, rescale)) {
+          const float alpha = rescale ? fast_exp2(m_used - m_cand) : 1.f;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 128; c += 32) {
+            float ot[32];
+            tmem_ld32(t_lane + 256 + c, ot);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ot[i] *= alpha;
+            tmem_st32(t_lane + 256 + c, ot);
+          }
+          if (rescale) l *= alpha;
+        }
+        if (rescale || m_used == kNegInf) m_used = m_cand;
+        const float neg_m = -m_used;
+        float sum = 0.f;
+        // P row t, 8 keys per 16-byte chunk: keys 0-63 in slab 0, 64-127 in slab 1, chunks swizzled by row
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          float pv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float x = s[8 * c + i];
+            pv[i] = x == kNegInf ? 0.f : fast_exp2(fmaf(x, p.scale_log2, neg_m));
+            sum += pv[i];
+          }
+          const uint4 v = make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]), pack_bf16x2(pv[4], pv[5]),
+                                     pack_bf16x2(pv[6], pv[7]));
+          *reinterpret_cast<uint4*>(smem + kOffP + (c >> 3) * kSlab + sw128_offset(t, c & 7)) = v;
+        }
+        l += sum;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bars[B_PFULL]);
+      }
+      if (!alive) break;
+      // ---- epilogue: O / l for the tile's valid rows
+      alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
+      if (!alive) break;
+      pv_seen = g;
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = p.out + (int64_t)(q0 + qt * 128 + t) * p.out_row_stride + (int64_t)h * kHeadDim;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        float ot[32];
+        tmem_ld32(t_lane + 256 + c, ot);
+        if (t < rows) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = pack_bf16x2(ot[i] * inv, ot[i + 1] * inv);
+            v.y = pack_bf16x2(ot[i + 2] * inv, ot[i + 3] * inv);
+            v.z = pack_bf16x2(ot[i + 4] * inv, ot[i + 5] * inv);
+            v.w = pack_bf16x2(ot[i + 6] * inv, ot[i + 7] * inv);
+            *reinterpret_cast<uint4*>(dst + c + i) = v;
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  }
+
+  __syncthreads();
+  if (*abort) {
+    if (tid == 0) atomicOr(&g_error_word, kErrTimeout);
+    for (int i = 0; i < 1000; ++i) sleep_ns(1000);
+    __syncthreads();
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_prefill(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                           const PrefillParams& p, int grid, cudaStream_t stream) {
+  if (p.num_seqs > kMaxDecodeSeqs || p.q_tiles_bound > kMaxPrefillTiles) return cudaErrorInvalidValue;
+  prefill_plan_kernel<<<1, 1024, 0, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, p);
+  return cudaGetLastError();
+}
+
+}  // namespace nva

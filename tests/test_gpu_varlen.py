@@ -1,0 +1,147 @@
+"""GPU parity of varlen attention (flash_attn_varlen_func's role at attention.py:64-70): prefill without a prefix
+(contiguous K/V), chunked prefill over a paged prefix, the mixed prefill+decode batch of BASELINE config 4, and the
+Attention module itself driven through the Context, all against the FP32 oracle."""
+import pytest
+import torch
+
+import oracle
+from conftest import assert_attn_close
+
+pytestmark = pytest.mark.gpu
+
+
+def run_varlen(b, paged=True):
+    from nvattn import ops
+    if paged:
+        k, v, bt = b.k_cache, b.v_cache, b.block_tables
+    else:
+        k, v, bt = b.k_new, b.v_new, None
+    return ops.flash_attn_varlen_func(b.q, k, v, max_seqlen_q=b.max_seqlen_q, cu_seqlens_q=b.cu_seqlens_q,
+                                      max_seqlen_k=b.max_seqlen_k, cu_seqlens_k=b.cu_seqlens_k,
+                                      softmax_scale=b.scale, causal=True, block_table=bt)
+
+
+def ref_varlen(b, paged=True):
+    if paged:
+        return oracle.varlen_attention_ref(b.q.cpu(), None, None, b.cu_seqlens_q.cpu(), b.cu_seqlens_k.cpu(),
+                                           b.scale, block_tables=b.block_tables.cpu(), k_cache=b.k_cache.cpu(),
+                                           v_cache=b.v_cache.cpu())
+    return oracle.varlen_attention_ref(b.q.cpu(), b.k_new.cpu(), b.v_new.cpu(), b.cu_seqlens_q.cpu(),
+                                       b.cu_seqlens_k.cpu(), b.scale)
+
+
+def batch(q_lens, k_lens, H=32, KVH=8, NB=512, seed=0, paged=True):
+    from nvattn.workloads import varlen_batch
+    return varlen_batch(q_lens, k_lens, H, KVH, 128, NB, 0.5, seed, device="cuda", paged=paged)
+
+
+@pytest.mark.parametrize("lens", [[1], [13], [64, 127, 128, 129], [300, 1, 1000, 5, 700]])
+def test_prefill_contiguous(cuda, lens):
+    """Prefill without a prefix: keys from the contiguous k/v rows (block_table None)."""
+    b = batch(lens, lens, seed=len(lens), paged=False)
+    assert_attn_close(run_varlen(b, paged=False), ref_varlen(b, paged=False), f"contiguous {lens}")
+
+
+@pytest.mark.parametrize("q_lens,prefix", [([200], [0]), ([512, 640, 640], [0, 256, 1024]),
+                                           ([129, 300, 77], [1, 383, 2000])])
+def test_prefill_paged_prefix(cuda, q_lens, prefix):
+    """Chunked prefill / prefix-cache hits: keys [0, prefix + q) from the paged cache."""
+    k_lens = [q + p for q, p in zip(q_lens, prefix)]
+    b = batch(q_lens, k_lens, seed=7)
+    assert_attn_close(run_varlen(b), ref_varlen(b), f"paged prefix {q_lens}/{prefix}")
+
+
+def test_varlen_decode_rows_only(cuda):
+    """A mixed step whose every run is short (decode rows with 1+k tokens): handled by the decode kernel."""
+    q_lens = [1] * 20 + [5] * 10 + [12] * 3
+    k_lens = [50 + 37 * i for i in range(len(q_lens))]
+    b = batch(q_lens, k_lens, seed=3)
+    assert_attn_close(run_varlen(b), ref_varlen(b), "varlen decode rows")
+
+
+def test_mixed_config4_full(cuda):
+    """256 decode rows (log-normal contexts) + prefill chunks 512/640/640 with prefixes
+    0/256/1024 in one varlen batch."""
+    from nvattn.workloads import mixed_config
+    b = mixed_config(seed=0, device="cuda")
+    assert_attn_close(run_varlen(b), ref_varlen(b), "config4")
+
+
+def test_mixed_group2_geometry(cuda):
+    """Qwen3-0.6B geometry (16 q heads, 8 kv heads: group 2) in a mixed batch: short runs up to 24 rows."""
+    q_lens = [1, 3, 24, 25, 300]
+    k_lens = [40, 300, 500, 600, 900]
+    b = batch(q_lens, k_lens, H=16, KVH=8, seed=11)
+    assert_attn_close(run_varlen(b), ref_varlen(b), "group 2")
+
+
+def test_prefill_stale_nan_past_context(cuda):
+    q_lens, k_lens = [300, 140], [300, 1100]
+    b = batch(q_lens, k_lens, seed=5)
+    ref = ref_varlen(b)
+    for i, L in enumerate(k_lens):
+        last = int(b.block_tables[i, (L + 255) // 256 - 1])
+        b.k_cache[last, L % 256 or 256:] = float("nan")
+        b.v_cache[last, L % 256 or 256:] = float("nan")
+    assert_attn_close(run_varlen(b), ref, "nan tail prefill")
+
+
+def test_attention_module_prefill_and_decode(cuda):
+    """nvattn.attention.Attention.forward reading the Context, as nano-vllm calls it: a prefill step (KV scattered
+    then attention over the contiguous k/v), then a prefix-cache prefill step over the paged cache."""
+    from nvattn.attention import Attention
+    from nvattn.context import set_context, reset_context
+    from nvattn.workloads import varlen_batch
+    H, KVH = 32, 8
+    attn = Attention(H, 128, 128 ** -0.5, KVH)
+    # empty cache (warmup): no scatter, contiguous keys
+    lens = [100, 37]
+    b = varlen_batch(lens, lens, H, KVH, 128, 64, 0.5, 1, device="cuda", paged=False)
+    set_context(True, b.cu_seqlens_q, b.cu_seqlens_k, b.max_seqlen_q, b.max_seqlen_k, b.slot_mapping)
+    o = attn(b.q, b.k_new, b.v_new)
+    reset_context()
+    assert_attn_close(o, ref_varlen(b, paged=False), "module prefill")
+    # with a cache: the step's K/V are scattered first, then the paged prefix is read
+    q_lens, k_lens = [64, 200], [64 + 300, 200 + 20]
+    b = varlen_batch(q_lens, k_lens, H, KVH, 128, 64, 0.5, 2, device="cuda")
+    ref = ref_varlen(b)
+    kc, vc = b.k_cache.clone(), b.v_cache.clone()
+    kc.view(-1, KVH, 128)[b.slot_mapping.long()] = 0     # the step's rows are not there yet
+    vc.view(-1, KVH, 128)[b.slot_mapping.long()] = 0
+    attn.k_cache, attn.v_cache = kc, vc
+    set_context(True, b.cu_seqlens_q, b.cu_seqlens_k, b.max_seqlen_q, b.max_seqlen_k, b.slot_mapping, None,
+                b.block_tables)
+    o = attn(b.q, b.k_new, b.v_new)
+    reset_context()
+    assert torch.equal(kc, b.k_cache) and torch.equal(vc, b.v_cache)
+    assert_attn_close(o, ref, "module prefix prefill")
+
+
+def test_attention_module_decode_graph(cuda):
+    """The decode branch of Attention.forward captured in a CUDA graph (ModelRunner.capture_cudagraph) and replayed
+    with new static inputs."""
+    from nvattn.attention import Attention
+    from nvattn.context import set_context, reset_context
+    from nvattn.workloads import paged_decode_batch
+    H, KVH, n = 32, 8, 3
+    b = paged_decode_batch([500, 1200, 31], n, H, KVH, 128, 64, 0.5, 9, device="cuda")
+    attn = Attention(H, 128, b.scale, KVH)
+    attn.k_cache, attn.v_cache = b.k_cache, b.v_cache
+    q, k, v = b.q.clone(), b.k_new.clone(), b.v_new.clone()
+    set_context(False, slot_mapping=b.slot_mapping, context_lens=b.context_lens, block_tables=b.block_tables)
+    eager = attn(q, k, v).clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        attn(q, k, v)
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = attn(q, k, v)
+    reset_context()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    ref = oracle.paged_attention_ref(b.q.cpu().view(3, n, H, 128), b.k_cache.cpu(), b.v_cache.cpu(),
+                                     b.context_lens.cpu(), b.block_tables.cpu(), b.scale)
+    assert_attn_close(out.view(3, n, H, 128), ref, "graph decode")
