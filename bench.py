@@ -292,6 +292,7 @@ def run_nvattn(args, world, rank, local):
                                      "us": round(v_ms * 1e3, 2),
                                      "TFLOPs": round(world * flops_decode(vl, k + 1, H) / (v_ms * 1e-3) / 1e12, 1)}
         del vb, vq, vout
+    secondary.update(varlen_rows(world, rank, args, flush, pk))
     from nvattn.workloads import accept_config
     t_ids, d_ids, nd = (x.cuda() for x in accept_config(8, S=32, seed=args.seed))
     acc_out = {}
@@ -328,6 +329,60 @@ def run_nvattn(args, world, rank, local):
         line["cpu_baseline"] = cpu_baseline(args.seed, budget_s=args.cpu_budget)
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def prefill_flops(q_lens, k_lens, H, D=128):
+    """Causal prefill FLOPs: 4*H*D per visible (query, key) pair; query i of a run of q sees k - q + i + 1 keys."""
+    pairs = sum(q * (k - q) + q * (q + 1) // 2 for q, k in zip(q_lens, k_lens))
+    return 4.0 * H * D * pairs
+
+
+def varlen_rows(world, rank, args, flush, pk):
+    """BASELINE config 4 rows at this rank's head shard: the prefill chunks alone (paged prefix, tensor-core bound),
+    a 2048-token prefill without prefix (contiguous K/V), and the whole mixed step (decode rows HBM-bound)."""
+    from nvattn import ops
+    from nvattn.workloads import mixed_config, varlen_batch
+    H, KVH = 32 // world, 8 // world
+    rows = {}
+
+    def timed(b, paged):
+        k, v, bt = (b.k_cache, b.v_cache, b.block_tables) if paged else (b.k_new, b.v_new, None)
+        out = torch.empty_like(b.q)
+
+        def call():
+            ops.flash_attn_varlen_func(b.q, k, v, max_seqlen_q=b.max_seqlen_q, cu_seqlens_q=b.cu_seqlens_q,
+                                       max_seqlen_k=b.max_seqlen_k, cu_seqlens_k=b.cu_seqlens_k,
+                                       softmax_scale=b.scale, causal=True, block_table=bt, out=out)
+        t = time_steps(capture(call).replay, max(10, args.steps // 2), args.warmup, flush)
+        return max_over_ranks(statistics.mean(t), world)
+
+    chunks, prefixes = [512, 640, 640], [0, 256, 1024]
+    kl = [c + p for c, p in zip(chunks, prefixes)]
+    b = varlen_batch(chunks, kl, H, KVH, 128, 64, 0.5, args.seed + 40, device="cuda")
+    ms = timed(b, True)
+    fl = prefill_flops(chunks, kl, H)
+    rows["prefill_config4_chunks"] = {"us": round(ms * 1e3, 2), "TFLOPs": round(world * fl / (ms * 1e-3) / 1e12, 1),
+                                      "frac_bf16": round(fl / (ms * 1e-3) / 1e12 / pk["bf16"], 3),
+                                      "GFLOP_per_rank": round(fl / 1e9, 2)}
+    del b
+    lens = [512] * 4
+    b = varlen_batch(lens, lens, H, KVH, 128, 64, 0.5, args.seed + 41, device="cuda", paged=False)
+    ms = timed(b, False)
+    fl = prefill_flops(lens, lens, H)
+    rows["prefill_4x512_contiguous"] = {"us": round(ms * 1e3, 2), "TFLOPs": round(world * fl / (ms * 1e-3) / 1e12, 1),
+                                        "frac_bf16": round(fl / (ms * 1e-3) / 1e12 / pk["bf16"], 3)}
+    del b
+    b = mixed_config(seed=args.seed, device="cuda", num_heads=H, num_kv_heads=KVH)
+    ms = timed(b, True)
+    nd = b.meta["num_decode"]
+    dec_bytes = attn_bytes(b.meta["k_lens"][:nd], 1, H, KVH)
+    fl = prefill_flops(b.meta["q_lens"][nd:], b.meta["k_lens"][nd:], H)
+    bound_us = max(fl / (pk["bf16"] * 1e12), dec_bytes / (pk["hbm"] * 1e9)) * 1e6
+    rows["mixed_config4"] = {"us": round(ms * 1e3, 2), "roofline_us": round(bound_us, 2),
+                             "frac_of_roofline": round(bound_us / (ms * 1e3), 3),
+                             "decode_part_MB": round(dec_bytes / 1e6, 1), "prefill_part_GFLOP": round(fl / 1e9, 2)}
+    del b
+    return rows
 
 
 def cpu_sample(seed, nseq):

@@ -22,6 +22,8 @@
 //   2 = Q loader: gathers a segment's rows into the swizzled operand layout (cp.async, zero-filled padding);
 //   4..7 = softmax: thread ct owns TMEM lane ct (token ct of S^T, dim ct of O^T).  Column maxima and sums over
 //       the 128 tokens use a transposed butterfly (each shuffle stage halves the rows a lane carries).
+#include <type_traits>
+
 #include "nva_ptx.cuh"
 #include "nva_kernels.h"
 
@@ -183,23 +185,42 @@ __device__ __forceinline__ void column_reduce(float* v, float* dst, int lane) {
   if ((lane & (kRep - 1)) == 0) dst[lane / kRep] = v[0];
 }
 
-// Column reduction of NP (16, 32 or 48) values per thread within one warp into dst[0..NP).
-template <int NP, bool kMax>
+// Column reduction of NR (8, 16, 32 or 48) values per thread within one warp into dst[0..NR).
+template <int NR, bool kMax>
 __device__ __forceinline__ void warp_columns(const float* x, float* dst, int lane) {
   float v[32];
-  if constexpr (NP == 16) {
+  if constexpr (NR <= 16) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = x[i];
-    column_reduce<16, kMax>(v, dst, lane);
+    for (int i = 0; i < NR; ++i) v[i] = x[i];
+    column_reduce<NR, kMax>(v, dst, lane);
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = x[i];
     column_reduce<32, kMax>(v, dst, lane);
-    if constexpr (NP == 48) {
+    if constexpr (NR == 48) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = x[32 + i];
       column_reduce<16, kMax>(v, dst + 32, lane);
     }
+  }
+}
+
+// Rows a segment carries through the softmax: its real rows rounded up to 8, 16, 32 or 48 (never above NP).
+__device__ __forceinline__ int rows_width(int R) { return R <= 8 ? 8 : R <= 16 ? 16 : R <= 32 ? 32 : 48; }
+// UMMA N for a segment (M = 128 needs N to be a multiple of 16).
+__device__ __forceinline__ int mma_width(int R) { return R <= 16 ? 16 : R <= 32 ? 32 : 48; }
+
+// Calls f(integral_constant<NR>) for the row width nr, limited to the kernel's NP.
+template <int NP, class F>
+__device__ __forceinline__ void with_rows(int nr, F&& f) {
+  if (nr <= 8) {
+    f(std::integral_constant<int, 8>{});
+  } else if (nr <= 16 || NP == 16) {
+    f(std::integral_constant<int, 16>{});
+  } else if (nr <= 32 || NP == 32) {
+    f(std::integral_constant<int, (NP >= 32 ? 32 : 16)>{});
+  } else {
+    f(std::integral_constant<int, NP>{});
   }
 }
 
@@ -260,6 +281,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   build_prefix(p, prefix, warp_tot, tid, kThreads);   // ends with __syncthreads
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // let the combine kernel (launched as a programmatic dependent) get resident and run its prologue now; it waits
+  // for this grid to finish before it reads any partial
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const int total = KVH * prefix[p.num_seqs];
   const int per = total > 0 ? (total + gridDim.x - 1) / gridDim.x : 1;
@@ -329,8 +353,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     }
   } else if (warp == 1 && ntiles > 0) {
     // ------------------------------------------------------------ UMMA issuer (whole warp polls, lane 0 issues)
-    constexpr uint32_t idesc_qk = umma_idesc_bf16(128, NP, false, false);
-    constexpr uint32_t idesc_pv = umma_idesc_bf16(128, NP, true, true);
     const uint32_t q_base = smem_u32(smem + C::kQ);
     const uint32_t p_base = smem_u32(smem + C::kP);
     const uint32_t k_base = smem_u32(smem + C::kK);
@@ -343,6 +365,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         const int st = qk % kStages;
         if (all_ready(&bars[B_KFULL + st], (qk / kStages) & 1)) {
           const int flags = info[2 * (qk % kInfoRing)].w;
+          // UMMA N for this tile's segment: its rows rounded up to 16/32/48
+          const uint32_t idesc_qk =
+              umma_idesc_bf16(128, min(NP, mma_width(info[2 * (qk % kInfoRing) + 1].x * G)), false, false);
           const int qb = qseg % C::kQBuf;
           const bool q_ok = !(flags & 1) || all_ready(&bars[B_QFULL + qb], (qseg / C::kQBuf) & 1);
           const int buf = qk & 1;
@@ -371,6 +396,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       if (pv < qk) {
         const int st = pv % kStages;
         if (all_ready(&bars[B_PFULL], pv & 1) && all_ready(&bars[B_VFULL + st], (pv / kStages) & 1)) {
+          const uint32_t idesc_pv =
+              umma_idesc_bf16(128, min(NP, mma_width(info[2 * (pv % kInfoRing) + 1].x * G)), true, true);
           tc_fence_after();
           if (lane == 0) {
             const uint32_t vb = v_base + st * kTileBytes;
@@ -416,8 +443,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       if (!mbar_wait_warp(&bars[B_QEMPTY + qb], ((qi / C::kQBuf) & 1) ^ 1, abort)) break;
       const SeqShape ss = seq_shape(p, lc.b);
       const int R = ss.n * G;
+      const int rows = min(NP, mma_width(R));   // the rows the S product reads; those past R are zero
       uint8_t* qs = smem + C::kQ + qb * NP * 256;
-      for (int idx = lane; idx < NP * 16; idx += 32) {
+      for (int idx = lane; idx < rows * 16; idx += 32) {
         const int r = idx >> 4, c = idx & 15;
         const int rr = r < R ? r : 0;
         const int i = rr / G, h = rr - i * G;
@@ -435,14 +463,15 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   } else if (warp >= 4 && ntiles > 0) {
     // ------------------------------------------------------------ softmax / accumulation
     // Every wait here is warp-uniform and every named barrier ORs "gave up" across the four warps, so the
-    // warps leave the loop together if a wait expires (no warp can be left behind at a barrier).
+    // warps leave the loop together if a wait expires (no warp can be left behind at a barrier).  The barrier
+    // sequence is the same for every row width, so a warp that gave up still matches the others.
     const int ct = tid - kConsumerBase;       // TMEM lane: token ct of S^T, dim ct of O^T
     const int wq = ct >> 5;                   // lane quadrant
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     const float inv_g = 1.0f / static_cast<float>(G);
     uint8_t* p_smem = smem + C::kP;
     float l[NP], o[NP], s[NP];
-    int R = 0, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0;
+    int R = 0, nr = 8, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0;
     bool alive = true;
     for (int jj = 0; jj < ntiles; ++jj) {
       const int st = jj % kStages;
@@ -459,6 +488,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         q0 = sh.z;
         seg_g = inf.y;
         R = n * G;
+        nr = min(NP, rows_width(R));
         seg_s0 = KVH * prefix[inf.x] + seg_g * sh.w;
         seg_s1 = seg_s0 + sh.w;
 #pragma unroll
@@ -486,22 +516,27 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       alive = alive && mbar_wait_warp(&bars[B_SFULL + buf], (jj >> 1) & 1, abort);
       if (alive) {
         tc_fence_after();
+        // query i of the segment sees tokens <= L - n + i, i.e. row r = i*G + h is visible iff r >= G*(tok-L+n)
+        const int d = tok - (L - n);
+        const int rmin = d > 0 ? d * G : 0;
+        with_rows<NP>(nr, [&](auto nr_c) {
+          constexpr int NR = decltype(nr_c)::value;
+          if constexpr (NR == 8) {
+            tmem_ld8(t_lane + buf * NP, s);
+          } else {
 #pragma unroll
-        for (int c = 0; c < NP; c += 16) tmem_ld16(t_lane + buf * NP + c, s + c);
-        tc_fence_before();
-        mbar_arrive(&bars[B_SEMPTY + buf]);
-        const int lim = L - n;   // query i sees tokens <= lim + i
+            for (int c = 0; c < NR; c += 16) tmem_ld16(t_lane + buf * NP + c, s + c);
+          }
+          tc_fence_before();
+          mbar_arrive(&bars[B_SEMPTY + buf]);
 #pragma unroll
-        for (int r = 0; r < NP; ++r) {
-          const int qrow = __float2int_rz((static_cast<float>(r) + 0.5f) * inv_g);
-          const bool vis = r < R && tok <= lim + qrow;
-          s[r] = vis ? s[r] * p.scale_log2 : kNegInf;
-        }
-        warp_columns<NP, true>(s, red + (buf * 4 + wq) * NP, lane);
+          for (int r = 0; r < NR; ++r) s[r] = (r >= rmin && r < R) ? s[r] * p.scale_log2 : kNegInf;
+          warp_columns<NR, true>(s, red + (buf * 4 + wq) * NP, lane);
+        });
       }
       if (named_bar_any(1, 128, !alive)) break;
       // ---- running max (one owner thread per row) and rescale factor
-      if (ct < NP) {
+      if (ct < nr) {
         float mn = 0.f, alpha = 1.f;
         if (ct < R) {
           const float* rr = red + buf * 4 * NP;
@@ -514,76 +549,105 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         alpha_s[buf * NP + ct] = alpha;
       }
       named_bar_sync(1, 128);
+      with_rows<NP>(nr, [&](auto nr_c) {
+        constexpr int NR = decltype(nr_c)::value;
+        const float* ms = m_s;
+        const float* al = alpha_s + buf * NP;
 #pragma unroll
-      for (int r = 0; r < NP; ++r) {
-        const float pr = (s[r] == kNegInf) ? 0.f : fast_exp2(s[r] - m_s[r]);
-        l[r] = l[r] * alpha_s[buf * NP + r] + pr;
-        s[r] = pr;
-      }
-      // ---- fold the previous tile's O; PV of tile jj-1 must also be done before P is overwritten
-      if (!first) {
-        alive = mbar_wait_warp(&bars[B_OFULL], (jj - 1) & 1, abort);
-        if (alive) {
-          tc_fence_after();
-          float ot[16];
+        for (int r = 0; r < NR; r += 4) {
+          const float4 m4 = *reinterpret_cast<const float4*>(ms + r);
+          const float4 a4 = *reinterpret_cast<const float4*>(al + r);
+          const float mv[4] = {m4.x, m4.y, m4.z, m4.w}, av[4] = {a4.x, a4.y, a4.z, a4.w};
 #pragma unroll
-          for (int c = 0; c < NP; c += 16) {
-            tmem_ld16(t_lane + 2 * NP + c, ot);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * alpha_s[(buf ^ 1) * NP + c + i] + ot[i];
+          for (int i = 0; i < 4; ++i) {
+            const float pr = (s[r + i] == kNegInf) ? 0.f : fast_exp2(s[r + i] - mv[i]);
+            l[r + i] = l[r + i] * av[i] + pr;
+            s[r + i] = pr;
           }
-          tc_fence_before();
         }
-      }
-      // ---- P^T (bf16), MN-major without swizzle: 8 consecutive rows of token ct form one 16-byte vector
-      if (alive) {
-        uint8_t* pb = p_smem + ct * 16;
+        // ---- fold the previous tile's O; PV of tile jj-1 must also be done before P is overwritten
+        if (!first) {
+          alive = mbar_wait_warp(&bars[B_OFULL], (jj - 1) & 1, abort);
+          if (alive) {
+            tc_fence_after();
+            const float* ap = alpha_s + (buf ^ 1) * NP;
+            float ot[16];
+            if constexpr (NR == 8) {
+              tmem_ld8(t_lane + 2 * NP, ot);
 #pragma unroll
-        for (int m = 0; m < NP / 8; ++m) {
-          uint4 v;
-          v.x = pack_bf16x2(s[8 * m + 0], s[8 * m + 1]);
-          v.y = pack_bf16x2(s[8 * m + 2], s[8 * m + 3]);
-          v.z = pack_bf16x2(s[8 * m + 4], s[8 * m + 5]);
-          v.w = pack_bf16x2(s[8 * m + 6], s[8 * m + 7]);
-          *reinterpret_cast<uint4*>(pb + m * 2048) = v;
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&bars[B_PFULL]);
-      }
-      if (last && alive) {
-        alive = mbar_wait_warp(&bars[B_OFULL], jj & 1, abort);
-        if (alive) {
-          tc_fence_after();
-          float ot[16];
+              for (int i = 0; i < 8; ++i) o[i] = o[i] * ap[i] + ot[i];
+            } else {
 #pragma unroll
-          for (int c = 0; c < NP; c += 16) {
-            tmem_ld16(t_lane + 2 * NP + c, ot);
+              for (int c = 0; c < NR; c += 16) {
+                tmem_ld16(t_lane + 2 * NP + c, ot);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * alpha_s[buf * NP + c + i] + ot[i];
+                for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * ap[c + i] + ot[i];
+              }
+            }
+            tc_fence_before();
           }
-          tc_fence_before();
-          warp_columns<NP, false>(l, lred + wq * NP, lane);
         }
-      }
+        // ---- P^T (bf16), MN-major without swizzle: 8 consecutive rows of token ct form one 16-byte vector.
+        // Rows past NR (up to the UMMA N) are never read back: their O^T columns are ignored.
+        if (alive) {
+          uint8_t* pb = p_smem + ct * 16;
+#pragma unroll
+          for (int m = 0; m < NR / 8; ++m) {
+            uint4 v;
+            v.x = pack_bf16x2(s[8 * m + 0], s[8 * m + 1]);
+            v.y = pack_bf16x2(s[8 * m + 2], s[8 * m + 3]);
+            v.z = pack_bf16x2(s[8 * m + 4], s[8 * m + 5]);
+            v.w = pack_bf16x2(s[8 * m + 6], s[8 * m + 7]);
+            *reinterpret_cast<uint4*>(pb + m * 2048) = v;
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&bars[B_PFULL]);
+        }
+        if (last && alive) {
+          alive = mbar_wait_warp(&bars[B_OFULL], jj & 1, abort);
+          if (alive) {
+            tc_fence_after();
+            const float* ap = alpha_s + buf * NP;
+            float ot[16];
+            if constexpr (NR == 8) {
+              tmem_ld8(t_lane + 2 * NP, ot);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] = o[i] * ap[i] + ot[i];
+            } else {
+#pragma unroll
+              for (int c = 0; c < NR; c += 16) {
+                tmem_ld16(t_lane + 2 * NP + c, ot);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * ap[c + i] + ot[i];
+              }
+            }
+            tc_fence_before();
+            warp_columns<NR, false>(l, lred + wq * NP, lane);
+          }
+        }
+      });
       if (named_bar_any(1, 128, !alive)) break;
       if (last) {
         const bool complete = (seg_s0 / per) == ((seg_s1 - 1) / per);
         const int slot = 2 * blockIdx.x + (seg_s0 < t_begin ? 0 : 1);
+        with_rows<NP>(nr, [&](auto nr_c) {
+          constexpr int NR = decltype(nr_c)::value;
 #pragma unroll
-        for (int r = 0; r < NP; ++r) {
-          if (r < R) {
-            const float lt = lred[r] + lred[NP + r] + lred[2 * NP + r] + lred[3 * NP + r];
-            const float val = lt > 0.f ? o[r] / lt : 0.f;
-            if (complete) {
-              const int i = __float2int_rz((static_cast<float>(r) + 0.5f) * inv_g), h = r - i * G;
-              p.out[(int64_t)(q0 + i) * p.out_row_stride + (int64_t)(seg_g * G + h) * kHeadDim + ct] =
-                  __float2bfloat16_rn(val);
-            } else {
-              p.part_o[((int64_t)slot * NP + r) * kHeadDim + ct] = val;
-              if (ct == 0) p.part_lse[slot * NP + r] = lt > 0.f ? m_s[r] + __log2f(lt) : kNegInf;
+          for (int r = 0; r < NR; ++r) {
+            if (r < R) {
+              const float lt = lred[r] + lred[NP + r] + lred[2 * NP + r] + lred[3 * NP + r];
+              const float val = lt > 0.f ? o[r] / lt : 0.f;
+              if (complete) {
+                const int i = __float2int_rz((static_cast<float>(r) + 0.5f) * inv_g), h = r - i * G;
+                p.out[(int64_t)(q0 + i) * p.out_row_stride + (int64_t)(seg_g * G + h) * kHeadDim + ct] =
+                    __float2bfloat16_rn(val);
+              } else {
+                p.part_o[((int64_t)slot * NP + r) * kHeadDim + ct] = val;
+                if (ct == 0) p.part_lse[slot * NP + r] = lt > 0.f ? m_s[r] + __log2f(lt) : kNegInf;
+              }
             }
           }
-        }
+        });
       }
     }
   }
@@ -610,6 +674,8 @@ paged_decode_combine(const DecodeParams p, int main_grid) {
   __shared__ int warp_tot[8];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   build_prefix(p, prefix, warp_tot, tid, 256);
+  // everything below reads the main kernel's partials or writes the output: wait for that grid to complete
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int KVH = p.num_kv_heads, G = p.group;
   // zero-length sequences (batch padding): their rows see no key, output 0
   for (int b = blockIdx.x; b < p.num_seqs; b += gridDim.x) {
@@ -678,7 +744,19 @@ cudaError_t launch_np(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const De
   paged_decode_kernel<NP><<<grid, kThreads, smem, stream>>>(tm_k, tm_v, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  paged_decode_combine<NP><<<grid, 256, 0, stream>>>(p, grid);
+  // programmatic dependent launch: the combine kernel's launch and prologue overlap the main kernel's tail
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, paged_decode_combine<NP>, p, grid);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -360,17 +360,22 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         tc_fence_before();
         mbar_arrive(&bars[B_SEMPTY + st]);
         const int kmax = lim - j * 128;          // columns > kmax are masked for this row
-        float mx = kNegInf;
+        // row maximum with 8 independent partial maxima (one softmax warp per SM quarter: ILP hides latency)
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = kNegInf;
         if (kmax >= 127) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c) mx = fmaxf(mx, s[c]);
+          for (int c = 0; c < 128; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
         } else {
 #pragma unroll
           for (int c = 0; c < 128; ++c) {
             s[c] = c <= kmax ? s[c] : kNegInf;
-            mx = fmaxf(mx, s[c]);
+            m8[c & 7] = fmaxf(m8[c & 7], s[c]);
           }
         }
+        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         const float m_cand = fmaxf(m_used, mx * p.scale_log2);
         const bool rescale = m_used != kNegInf && m_cand > m_used + kRescaleLog2;
         // P buffer reuse and any O rescale both need the previous PV product complete
@@ -394,7 +399,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         }
         if (rescale || m_used == kNegInf) m_used = m_cand;
         const float neg_m = -m_used;
-        float sum = 0.f;
+        float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         // P row t, 8 keys per 16-byte chunk: keys 0-63 in slab 0, 64-127 in slab 1, chunks swizzled by row
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
@@ -403,13 +408,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           for (int i = 0; i < 8; ++i) {
             const float x = s[8 * c + i];
             pv[i] = x == kNegInf ? 0.f : fast_exp2(fmaf(x, p.scale_log2, neg_m));
-            sum += pv[i];
+            sum8[i] += pv[i];
           }
           const uint4 v = make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]), pack_bf16x2(pv[4], pv[5]),
                                      pack_bf16x2(pv[6], pv[7]));
           *reinterpret_cast<uint4*>(smem + kOffP + (c >> 3) * kSlab + sw128_offset(t, c & 7)) = v;
         }
-        l += sum;
+        l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&bars[B_PFULL]);

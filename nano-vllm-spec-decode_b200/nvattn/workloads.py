@@ -207,3 +207,19 @@ def bytes_decode(lens, q_per_seq, num_heads, num_kv_heads, head_dim=128, elem=2)
     kv = sum(lens) * 2 * num_kv_heads * head_dim * elem
     qo = 2 * len(lens) * q_per_seq * num_heads * head_dim * elem
     return float(kv + qo)
+
+
+def shard_heads(b: PagedBatch, rank: int, world: int) -> PagedBatch:
+    """Rank `rank`'s tensor-parallel shard of a batch (qwen3.py:29-39 head split; model_runner.py:251 cache of
+    num_kv_heads // world heads): q heads [r*H/t, (r+1)*H/t) and kv heads [r*KVH/t, (r+1)*KVH/t).  The block tables,
+    slots and lengths are shared by all ranks."""
+    H, KVH = b.q.shape[1], b.k_cache.shape[2]
+    assert H % world == 0 and KVH % world == 0
+    h0, h1 = rank * H // world, (rank + 1) * H // world
+    k0, k1 = rank * KVH // world, (rank + 1) * KVH // world
+    return PagedBatch(q=b.q[:, h0:h1].contiguous(), k_new=b.k_new[:, k0:k1].contiguous(),
+                      v_new=b.v_new[:, k0:k1].contiguous(), k_cache=b.k_cache[:, :, k0:k1].contiguous(),
+                      v_cache=b.v_cache[:, :, k0:k1].contiguous(), slot_mapping=b.slot_mapping,
+                      block_tables=b.block_tables, context_lens=b.context_lens, cu_seqlens_q=b.cu_seqlens_q,
+                      cu_seqlens_k=b.cu_seqlens_k, max_seqlen_q=b.max_seqlen_q, max_seqlen_k=b.max_seqlen_k,
+                      q_per_seq=b.q_per_seq, scale=b.scale, meta=dict(b.meta, rank=rank, world=world))
