@@ -293,6 +293,7 @@ def run_nvattn(args, world, rank, local):
                                      "TFLOPs": round(world * flops_decode(vl, k + 1, H) / (v_ms * 1e-3) / 1e12, 1)}
         del vb, vq, vout
     secondary.update(varlen_rows(world, rank, args, flush, pk))
+    secondary["flash_attn_2_8_3_same_workloads"] = fa2_rows(world, rank, args, flush, b, q4, lens, H, KVH)
     from nvattn.workloads import accept_config
     t_ids, d_ids, nd = (x.cuda() for x in accept_config(8, S=32, seed=args.seed))
     acc_out = {}
@@ -382,6 +383,40 @@ def varlen_rows(world, rank, args, flush, pk):
                              "frac_of_roofline": round(bound_us / (ms * 1e3), 3),
                              "decode_part_MB": round(dec_bytes / 1e6, 1), "prefill_part_GFLOP": round(fl / 1e9, 2)}
     del b
+    return rows
+
+
+def fa2_rows(world, rank, args, flush, b, q4, lens, H, KVH):
+    """The reference's own GPU attention (flash-attn 2.8.3, the calls of attention.py:67-77) on the same workloads,
+    same graph-replay timing: context for the numbers above, not part of this arm's measurement."""
+    try:
+        from flash_attn import flash_attn_varlen_func, flash_attn_with_kvcache
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    rows = {}
+    out = {}
+
+    def dec():
+        out["o"] = flash_attn_with_kvcache(q4, b.k_cache, b.v_cache, cache_seqlens=b.context_lens,
+                                           block_table=b.block_tables, softmax_scale=b.scale, causal=True)
+    t = time_steps(capture(dec).replay, max(10, args.steps // 2), args.warmup, flush)
+    ms = max_over_ranks(statistics.mean(t), world)
+    by = attn_bytes(lens, 1, H, KVH)
+    rows["decode_config2"] = {"us": round(ms * 1e3, 2), "GBps": round(world * by / (ms * 1e-3) / 1e9, 1)}
+    from nvattn.workloads import varlen_batch
+    chunks, prefixes = [512, 640, 640], [0, 256, 1024]
+    kl = [c + p for c, p in zip(chunks, prefixes)]
+    vb = varlen_batch(chunks, kl, H, KVH, 128, 64, 0.5, args.seed + 40, device="cuda")
+
+    def pre():
+        out["p"] = flash_attn_varlen_func(vb.q, vb.k_cache, vb.v_cache, max_seqlen_q=vb.max_seqlen_q,
+                                          cu_seqlens_q=vb.cu_seqlens_q, max_seqlen_k=vb.max_seqlen_k,
+                                          cu_seqlens_k=vb.cu_seqlens_k, softmax_scale=vb.scale, causal=True,
+                                          block_table=vb.block_tables)
+    t = time_steps(capture(pre).replay, max(10, args.steps // 2), args.warmup, flush)
+    ms = max_over_ranks(statistics.mean(t), world)
+    fl = prefill_flops(chunks, kl, H)
+    rows["prefill_config4_chunks"] = {"us": round(ms * 1e3, 2), "TFLOPs": round(world * fl / (ms * 1e-3) / 1e12, 1)}
     return rows
 
 

@@ -430,7 +430,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           __syncwarp();
           break;
         }
-        sleep_ns(32);
+        // nothing ready: sleep in hardware on the next PV input (softmax's P) or, with no PV pending, on the next
+        // K tile, for at most 64 ns; either completion wakes the warp at once
+        if (pv < qk) {
+          (void)mbar_try_wait_hint(&bars[B_PFULL], pv & 1, 64);
+        } else if (qk < ntiles) {
+          (void)mbar_try_wait_hint(&bars[B_KFULL + qk % kStages], (qk / kStages) & 1, 64);
+        }
+        __syncwarp();
       }
     }
   } else if (warp == 2 && ntiles > 0) {

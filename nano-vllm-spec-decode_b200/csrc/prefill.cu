@@ -318,7 +318,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           __syncwarp();
           break;
         }
-        sleep_ns(32);
+        // nothing ready: sleep in hardware (at most 64 ns) on the next PV input, else on the next K tile
+        if (gp < gq) {
+          (void)mbar_try_wait_hint(&bars[B_PFULL], gp & 1, 64);
+        } else if (it_q < my_items) {
+          (void)mbar_try_wait_hint(&bars[B_KFULL + (gq & 1)], (gq >> 1) & 1, 64);
+        }
+        __syncwarp();
       }
     }
   } else if (warp >= 4) {

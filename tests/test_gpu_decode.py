@@ -136,3 +136,24 @@ def test_no_device_error_after_runs(cuda):
     b = batch([300, 600], n=2, seed=8)
     run_decode(b)
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("name", ["decode", "verify_k3", "verify_k8_padded", "mixed_paged", "prefill_contiguous"])
+def test_kernels_match_flash_attn_golden(cuda, name):
+    """Our kernels against flash-attn 2.8.3's outputs (the reference's attention library) on the same inputs."""
+    from nvattn import ops
+    from test_oracle import fa2_case
+    kind, args, _, fa2_out = fa2_case(name)      # also puts tests/golden on sys.path
+    import make_golden_fa2 as mg
+    b = mg.build(kind, args, device="cuda")
+    if kind == "paged_decode":
+        B, n = b.num_seqs, b.q_per_seq
+        got = ops.flash_attn_with_kvcache(b.q.view(B, n, 8, 128), b.k_cache, b.v_cache, cache_seqlens=b.context_lens,
+                                          block_table=b.block_tables, softmax_scale=b.scale).reshape(B * n, 8, 128)
+    else:
+        paged = b.meta["paged"]
+        k, v, bt = (b.k_cache, b.v_cache, b.block_tables) if paged else (b.k_new, b.v_new, None)
+        got = ops.flash_attn_varlen_func(b.q, k, v, max_seqlen_q=b.max_seqlen_q, cu_seqlens_q=b.cu_seqlens_q,
+                                         max_seqlen_k=b.max_seqlen_k, cu_seqlens_k=b.cu_seqlens_k,
+                                         softmax_scale=b.scale, causal=True, block_table=bt)
+    assert_attn_close(got, fa2_out.float(), f"kernels vs flash-attn: {name}")

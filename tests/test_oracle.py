@@ -129,3 +129,54 @@ def test_config1_slots_follow_block_rule():
         assert int(b.slot_mapping[i]) == int(b.block_tables[i, p // 256]) * 256 + p % 256
     used = [int(x) for row in b.block_tables for x in row if x >= 0]
     assert len(used) == len(set(used)) and all(0 <= x < 64 for x in used)
+
+
+# ------------------------------------------------------------------ attention pinned to flash-attn 2.8.3
+FA2 = None
+
+
+def _fa2():
+    global FA2
+    if FA2 is None:
+        import numpy as np
+        import os
+        from conftest import REPO
+        z = np.load(os.path.join(REPO, "tests", "golden", "attention_fa2_golden.npz"))
+        FA2 = {k: z[k] for k in z.files}
+    return FA2
+
+
+def fa2_case(name):
+    """(inputs rebuilt from the generator's seed, flash-attn's bf16 output) for one golden case."""
+    import sys
+    import os
+    from conftest import REPO
+    sys.path.insert(0, os.path.join(REPO, "tests", "golden"))
+    import make_golden_fa2 as mg
+    kind, args = next((k, a) for n, k, a in mg.CASES if n == name)
+    b = mg.build(kind, args)
+    g = _fa2()
+    assert np.allclose(mg.checksum(b), g[f"{name}/checksum"], rtol=1e-9, atol=1e-6), "regenerated inputs drifted"
+    out = torch.from_numpy(g[f"{name}/out"].view(np.int16).copy()).view(torch.bfloat16)
+    return kind, args, b, out
+
+
+FA2_CASES = ["decode", "verify_k3", "verify_k8_padded", "mixed_paged", "prefill_contiguous"]
+
+
+@pytest.mark.parametrize("name", FA2_CASES)
+def test_attention_oracle_matches_flash_attn(name):
+    """The FP32 restatement against the reference's own attention library (flash-attn 2.8.3 on B200, called as
+    attention.py calls it), within the bf16 tolerance: pins the attention oracle."""
+    from conftest import assert_attn_close
+    kind, args, b, out = fa2_case(name)
+    if kind == "paged_decode":
+        B, n = b.num_seqs, b.q_per_seq
+        ref = oracle.paged_attention_ref(b.q.view(B, n, 8, 128), b.k_cache, b.v_cache, b.context_lens,
+                                         b.block_tables, b.scale).reshape(B * n, 8, 128)
+    elif b.meta["paged"]:
+        ref = oracle.varlen_attention_ref(b.q, None, None, b.cu_seqlens_q, b.cu_seqlens_k, b.scale,
+                                          block_tables=b.block_tables, k_cache=b.k_cache, v_cache=b.v_cache)
+    else:
+        ref = oracle.varlen_attention_ref(b.q, b.k_new, b.v_new, b.cu_seqlens_q, b.cu_seqlens_k, b.scale)
+    assert_attn_close(out, ref, f"flash-attn vs oracle: {name}")
