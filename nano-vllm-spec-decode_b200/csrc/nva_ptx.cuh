@@ -294,6 +294,37 @@ __device__ __forceinline__ void umma_bf16_ss(uint32_t d_tmem, uint64_t adesc, ui
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]^T: A (M x K, bf16) read from tensor memory, row m in lane m, two consecutive K
+// elements per 32-bit column (lower half = even element).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Eight K=16 steps of one product, D (+)= A * B^T, from shared-memory descriptors.  a_step / b_step advance each
+// descriptor's start-address field (16-byte units) per step: {a,b}_step[i] = byte offset of step i >> 4, with the
+// offsets of steps 4..7 allowed to jump to a second slab.  The first step overwrites D unless `accumulate`.
+__device__ __forceinline__ void umma_bf16_ss_x8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate, const uint32_t (&a_off)[8],
+                                                const uint32_t (&b_off)[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint64_t a = adesc + a_off[k];
+    const uint64_t b = bdesc + b_off[k];
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(k > 0 ? 1u : accumulate)
+        : "memory");
+  }
+}
+
 // Arrive once on `bar` when all previously issued tcgen05 ops of this thread have completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -353,92 +353,63 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     }
   } else if (warp == 1 && ntiles > 0) {
     // ------------------------------------------------------------ UMMA issuer (whole warp polls, lane 0 issues)
-    const uint32_t q_base = smem_u32(smem + C::kQ);
-    const uint32_t p_base = smem_u32(smem + C::kP);
-    const uint32_t k_base = smem_u32(smem + C::kK);
-    const uint32_t v_base = smem_u32(smem + C::kV);
+    const uint64_t q_desc0 = umma_desc_sw128(smem_u32(smem + C::kQ), 16, 1024);
+    const uint64_t k_desc0 = umma_desc_sw128(smem_u32(smem + C::kK), 16, 1024);
+    const uint64_t v_desc0 = umma_desc_sw128(smem_u32(smem + C::kV), kSlab, 1024);
+    const uint64_t p_desc0 = umma_desc_noswz(smem_u32(smem + C::kP), 128, 2048);
+    // Issue order: QK(0), QK(1), then PV(j), QK(j+2), ...  The softmax warps find S(j+1) ready when they finish
+    // tile j, and every wait is a blocking, hardware-suspended mbarrier wait (no polling next to a softmax warp).
     int qk = 0, pv = 0, qseg = 0;
-    uint64_t last_progress = globaltimer();
-    while (pv < ntiles) {
-      bool did = false;
-      if (qk < ntiles) {
-        const int st = qk % kStages;
-        if (all_ready(&bars[B_KFULL + st], (qk / kStages) & 1)) {
-          const int flags = info[2 * (qk % kInfoRing)].w;
-          // UMMA N for this tile's segment: its rows rounded up to 16/32/48
-          const uint32_t idesc_qk =
-              umma_idesc_bf16(128, min(NP, mma_width(info[2 * (qk % kInfoRing) + 1].x * G)), false, false);
-          const int qb = qseg % C::kQBuf;
-          const bool q_ok = !(flags & 1) || all_ready(&bars[B_QFULL + qb], (qseg / C::kQBuf) & 1);
-          const int buf = qk & 1;
-          if (q_ok && all_ready(&bars[B_SEMPTY + buf], ((qk >> 1) & 1) ^ 1)) {
-            tc_fence_after();
-            if (lane == 0) {
-              const uint32_t kb = k_base + st * kTileBytes;
-              const uint32_t qbuf = q_base + qb * NP * 256;
-#pragma unroll
-              for (int k = 0; k < 8; ++k) {
-                const uint64_t a = umma_desc_sw128(kb + (k >> 2) * kSlab + (k & 3) * 32, 16, 1024);
-                const uint64_t bq = umma_desc_sw128(qbuf + (k >> 2) * (NP * 128) + (k & 3) * 32, 16, 1024);
-                umma_bf16_ss(tmem + buf * NP, a, bq, idesc_qk, k > 0);
-              }
-              umma_commit(&bars[B_SFULL + buf]);
-              umma_commit(&bars[B_KEMPTY + st]);
-              if (flags & 2) umma_commit(&bars[B_QEMPTY + qb]);
-            }
-            __syncwarp();
-            if (flags & 2) ++qseg;
-            ++qk;
-            did = true;
-          }
-        }
+    bool ok = true;
+    auto issue_qk = [&]() {
+      if (!ok || qk >= ntiles) return;
+      const int st = qk % kStages;
+      const int e = qk % kInfoRing;
+      if (!mbar_wait_warp(&bars[B_KFULL + st], (qk / kStages) & 1, abort)) { ok = false; return; }
+      const int flags = info[2 * e].w;
+      // UMMA N for this tile's segment: its rows rounded up to 16/32/48
+      const uint32_t idesc_qk = umma_idesc_bf16(128, min(NP, mma_width(info[2 * e + 1].x * G)), false, false);
+      const int qb = qseg % C::kQBuf;
+      if ((flags & 1) && !mbar_wait_warp(&bars[B_QFULL + qb], (qseg / C::kQBuf) & 1, abort)) { ok = false; return; }
+      const int buf = qk & 1;
+      if (!mbar_wait_warp(&bars[B_SEMPTY + buf], ((qk >> 1) & 1) ^ 1, abort)) { ok = false; return; }
+      tc_fence_after();
+      if (lane == 0) {
+        // K-major SW128 operands: step k at +32 B within a 128-byte row, steps 4..7 in the second slab
+        constexpr uint32_t kOffK[8] = {0, 2, 4, 6, kSlab >> 4, (kSlab >> 4) + 2, (kSlab >> 4) + 4, (kSlab >> 4) + 6};
+        constexpr uint32_t kOffQ[8] = {0, 2, 4, 6, (NP * 128) >> 4, ((NP * 128) >> 4) + 2, ((NP * 128) >> 4) + 4,
+                                       ((NP * 128) >> 4) + 6};
+        umma_bf16_ss_x8(tmem + buf * NP, k_desc0 + ((st * kTileBytes) >> 4), q_desc0 + ((qb * NP * 256) >> 4),
+                        idesc_qk, 0u, kOffK, kOffQ);
+        umma_commit(&bars[B_SFULL + buf]);
+        umma_commit(&bars[B_KEMPTY + st]);
+        if (flags & 2) umma_commit(&bars[B_QEMPTY + qb]);
       }
-      if (pv < qk) {
-        const int st = pv % kStages;
-        if (all_ready(&bars[B_PFULL], pv & 1) && all_ready(&bars[B_VFULL + st], (pv / kStages) & 1)) {
-          const uint32_t idesc_pv =
-              umma_idesc_bf16(128, min(NP, mma_width(info[2 * (pv % kInfoRing) + 1].x * G)), true, true);
-          tc_fence_after();
-          if (lane == 0) {
-            const uint32_t vb = v_base + st * kTileBytes;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              // A = V^T: 16 tokens (two 8-row groups, SBO 1024) x 128 dims (two 64-dim slabs, LBO 16 KB)
-              const uint64_t a = umma_desc_sw128(vb + k * 2048, kSlab, 1024);
-              // B = P^T: 16 tokens (two 8-token core-matrix groups, LBO 128) x NP rows (8-row groups, SBO 2048)
-              const uint64_t bp = umma_desc_noswz(p_base + k * 256, 128, 2048);
-              umma_bf16_ss(tmem + 2 * NP, a, bp, idesc_pv, k > 0);
-            }
-            umma_commit(&bars[B_OFULL]);
-            umma_commit(&bars[B_VEMPTY + st]);
-          }
-          __syncwarp();
-          ++pv;
-          did = true;
-        }
+      __syncwarp();
+      if (flags & 2) ++qseg;
+      ++qk;
+    };
+    issue_qk();
+    issue_qk();
+    while (ok && pv < ntiles) {
+      const int st = pv % kStages;
+      if (!mbar_wait_warp(&bars[B_PFULL], pv & 1, abort)) break;
+      if (!mbar_wait_warp(&bars[B_VFULL + st], (pv / kStages) & 1, abort)) break;
+      const uint32_t idesc_pv =
+          umma_idesc_bf16(128, min(NP, mma_width(info[2 * (pv % kInfoRing) + 1].x * G)), true, true);
+      tc_fence_after();
+      if (lane == 0) {
+        // A = V^T: 16 tokens per step (two 8-row groups, SBO 1024; two 64-dim slabs, LBO 16 KB) -> +2048 B;
+        // B = P^T: 16 tokens per step (two 8-token core-matrix groups, LBO 128; 8-row groups, SBO 2048) -> +256 B
+        constexpr uint32_t kOffV[8] = {0, 128, 256, 384, 512, 640, 768, 896};
+        constexpr uint32_t kOffP[8] = {0, 16, 32, 48, 64, 80, 96, 112};
+        umma_bf16_ss_x8(tmem + 2 * NP, v_desc0 + ((st * kTileBytes) >> 4), p_desc0, idesc_pv, 0u, kOffV, kOffP);
+        umma_commit(&bars[B_OFULL]);
+        umma_commit(&bars[B_VEMPTY + st]);
       }
-      if (did) {
-        last_progress = globaltimer();
-      } else {
-        // warp-uniform decision to give up (the abort flag may be raised by another warp at any time)
-        const bool timed_out = globaltimer() - last_progress > kWaitLimitNs;
-        if (__any_sync(kFull, *abort != 0 || timed_out)) {
-          if (lane == 0 && *abort == 0) {
-            *abort = 1;
-            atomicOr(&g_error_word, kErrTimeout);
-          }
-          __syncwarp();
-          break;
-        }
-        // nothing ready: sleep in hardware on the next PV input (softmax's P) or, with no PV pending, on the next
-        // K tile, for at most 64 ns; either completion wakes the warp at once
-        if (pv < qk) {
-          (void)mbar_try_wait_hint(&bars[B_PFULL], pv & 1, 64);
-        } else if (qk < ntiles) {
-          (void)mbar_try_wait_hint(&bars[B_KFULL + qk % kStages], (qk / kStages) & 1, 64);
-        }
-        __syncwarp();
-      }
+      __syncwarp();
+      ++pv;
+      issue_qk();
     }
   } else if (warp == 2 && ntiles > 0) {
     // ------------------------------------------------------------ Q loader

@@ -6,8 +6,9 @@
 // long diagonal tiles start first and the short ones fill the tail.
 //
 // Per item: S = Q K^T with M = 128 query rows on the TMEM lanes, N = 128 keys (A = Q, B = K tile, both K-major
-// 128B-swizzled straight from TMA); P = exp2(S * scale - m) in bf16 through 128B-swizzled shared memory; O += P V in
-// TMEM (A = P, K-major; B = V tile, MN-major, straight from TMA).  One thread owns one query row: its maximum and sum
+// 128B-swizzled straight from TMA); P = exp2(S * scale - m) in bf16, written back into the first 64 columns of its
+// own S buffer in tensor memory; O += P V in TMEM (A = P read from TMEM, B = V tile, MN-major, straight from TMA).
+// Keeping P out of shared memory pays for a 3-stage V ring.  One thread owns one query row: its maximum and sum
 // are thread-local (no shuffles, no barriers between the softmax warps).  O is rescaled in TMEM only when a row's
 // maximum grows by more than 2^8 (until then P values up to 256 are exact enough in bf16 and FP32 sums).
 //
@@ -29,11 +30,12 @@ constexpr uint32_t kFull = 0xffffffffu;
 constexpr float kRescaleLog2 = 8.0f;   // rescale O only when a row maximum grows by more than this (log2 units)
 
 // shared memory map (offsets from a 1024-aligned base)
-constexpr int kOffQ = 0;                    // 2 x Q tile
-constexpr int kOffK = kOffQ + 2 * kTile;    // 2-stage K ring
-constexpr int kOffV = kOffK + 2 * kTile;    // 2-stage V ring
-constexpr int kOffP = kOffV + 2 * kTile;    // P tile
-constexpr int kOffBars = kOffP + kTile;     // 32 x u64
+constexpr int kKStages = 2;
+constexpr int kVStages = 3;
+constexpr int kOffQ = 0;                              // 2 x Q tile
+constexpr int kOffK = kOffQ + 2 * kTile;              // K ring
+constexpr int kOffV = kOffK + kKStages * kTile;       // V ring
+constexpr int kOffBars = kOffV + kVStages * kTile;    // 32 x u64
 constexpr int kOffItems = kOffBars + 32 * 8;      // kItemRing x 2 x int4
 constexpr int kOffTmem = kOffItems + kItemRing * 32;
 constexpr int kOffAbort = kOffTmem + 4;
@@ -41,8 +43,8 @@ constexpr int kSmemBytes = kOffAbort + 4 + 1024;
 static_assert(kSmemBytes <= 232448, "prefill shared memory budget");
 
 enum {
-  B_QFULL = 0, B_QEMPTY = 2, B_KFULL = 4, B_KEMPTY = 6, B_VFULL = 8, B_VEMPTY = 10, B_SFULL = 12, B_SEMPTY = 14,
-  B_PFULL = 16, B_ODONE = 17, B_ITEM = 18   // B_ITEM + kItemRing <= 32
+  B_QFULL = 0, B_QEMPTY = 2, B_KFULL = 4, B_KEMPTY = 6, B_VFULL = 8, B_VEMPTY = 11, B_SFULL = 14, B_PFULL = 16,
+  B_ODONE = 17, B_ITEM = 18   // B_ITEM + kItemRing <= 32
 };
 
 struct Item {
@@ -148,13 +150,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[B_QFULL + i], 1);
-      mbar_init(&bars[B_QEMPTY + i], 1);
+      mbar_init(&bars[B_QEMPTY + i], 128);   // released by the softmax threads after the item's epilogue
       mbar_init(&bars[B_KFULL + i], 1);
       mbar_init(&bars[B_KEMPTY + i], 1);
+      mbar_init(&bars[B_SFULL + i], 1);
+    }
+    for (int i = 0; i < kVStages; ++i) {
       mbar_init(&bars[B_VFULL + i], 1);
       mbar_init(&bars[B_VEMPTY + i], 1);
-      mbar_init(&bars[B_SFULL + i], 1);
-      mbar_init(&bars[B_SEMPTY + i], 128);
     }
     mbar_init(&bars[B_PFULL], 128);
     mbar_init(&bars[B_ODONE], 1);
@@ -183,6 +186,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     uint8_t* ring = smem + (is_k ? kOffK : kOffV);
     uint64_t* full = bars + (is_k ? B_KFULL : B_VFULL);
     uint64_t* empty = bars + (is_k ? B_KEMPTY : B_VEMPTY);
+    const int stages = is_k ? kKStages : kVStages;
     int g = 0, it_count = 0;
     bool stop = false;
     for (int k = blockIdx.x; k < n_items && !stop; k += gridDim.x, ++it_count) {
@@ -224,8 +228,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const int cnt = min(32, it.nkv - base);
         for (int i = 0; i < cnt; ++i, ++g) {
           const int r0 = __shfl_sync(kFull, row0, i);
-          const int st = g & 1;
-          if (!mbar_wait_warp(&empty[st], ((g >> 1) & 1) ^ 1, abort)) {
+          const int st = g % stages;
+          if (!mbar_wait_warp(&empty[st], ((g / stages) & 1) ^ 1, abort)) {
             stop = true;
             break;
           }
@@ -242,90 +246,68 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     // ------------------------------------------------------------ UMMA issuer
     constexpr uint32_t idesc_qk = umma_idesc_bf16(128, 128, false, false);
     constexpr uint32_t idesc_pv = umma_idesc_bf16(128, 128, false, true);
-    const uint32_t q_base = smem_u32(smem + kOffQ), k_base = smem_u32(smem + kOffK);
-    const uint32_t v_base = smem_u32(smem + kOffV), p_base = smem_u32(smem + kOffP);
-    // QK cursor (item, tile) and PV cursor (item, tile); item lengths come from the descriptor ring
-    int it_q = 0, j_q = 0, nkv_q = -1, gq = 0;
-    int it_p = 0, j_p = 0, nkv_p = -1, gp = 0;
+    const uint32_t v_base = smem_u32(smem + kOffV);
+    const uint64_t q_desc0 = umma_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
+    const uint64_t k_desc0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
+    const uint64_t v_desc0 = umma_desc_sw128(v_base, kSlab, 1024);
+    // Issue order: QK(0), QK(1), then PV(g), QK(g+2), ...  QK(g+2) overwrites the S buffer that holds P(g), so it
+    // must follow PV(g) (the tensor pipe runs one thread's products in issue order); every wait is a blocking,
+    // hardware-suspended mbarrier wait.  Tile indices g run across the CTA's items.
     const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    uint64_t last_progress = globaltimer();
-    while (it_p < my_items) {
-      bool did = false;
-      if (it_q < my_items) {
+    int it_q = 0, j_q = 0, nkv_q = 0, gq = 0;   // next S product
+    int it_p = 0, j_p = 0, gp = 0;              // next PV product
+    bool ok = true;
+    auto issue_qk = [&]() {
+      if (!ok || it_q >= my_items) return;
+      const int qb = it_q & 1;
+      if (j_q == 0) {
         const int e = it_q % kItemRing;
-        if (nkv_q < 0 && all_ready(&bars[B_ITEM + e], (it_q / kItemRing) & 1)) nkv_q = items[2 * e].w;
-        const int st = gq & 1, qb = it_q & 1;
-        if (nkv_q >= 0 && (j_q > 0 || all_ready(&bars[B_QFULL + qb], (it_q >> 1) & 1)) &&
-            all_ready(&bars[B_KFULL + st], (gq >> 1) & 1) && all_ready(&bars[B_SEMPTY + st], ((gq >> 1) & 1) ^ 1)) {
-          tc_fence_after();
-          if (lane == 0) {
-            const uint32_t qa = q_base + qb * kTile, kb = k_base + st * kTile;
+        if (!mbar_wait_warp(&bars[B_ITEM + e], (it_q / kItemRing) & 1, abort)) { ok = false; return; }
+        nkv_q = items[2 * e].w;
+        if (!mbar_wait_warp(&bars[B_QFULL + qb], (it_q >> 1) & 1, abort)) { ok = false; return; }
+      }
+      const int st = gq & 1;
+      if (!mbar_wait_warp(&bars[B_KFULL + st], (gq >> 1) & 1, abort)) { ok = false; return; }
+      tc_fence_after();
+      if (lane == 0) {
+        // K-major SW128 operands: step k sits at +32 B within a 128-byte row, steps 4..7 in the second slab
+        constexpr uint32_t kOff[8] = {0, 2, 4, 6, kSlab >> 4, (kSlab >> 4) + 2, (kSlab >> 4) + 4, (kSlab >> 4) + 6};
+        umma_bf16_ss_x8(tmem + st * 128, q_desc0 + ((qb * kTile) >> 4), k_desc0 + ((st * kTile) >> 4), idesc_qk, 0u,
+                        kOff, kOff);
+        umma_commit(&bars[B_SFULL + st]);
+        umma_commit(&bars[B_KEMPTY + st]);
+      }
+      __syncwarp();
+      ++gq;
+      if (++j_q == nkv_q) {
+        j_q = 0;
+        ++it_q;
+      }
+    };
+    issue_qk();
+    issue_qk();
+    while (ok && it_p < my_items) {
+      const int nkv_p = items[2 * (it_p % kItemRing)].w;   // published (and awaited) before this item's first QK
+      const int st = gp % kVStages;
+      if (!mbar_wait_warp(&bars[B_PFULL], gp & 1, abort)) break;
+      if (!mbar_wait_warp(&bars[B_VFULL + st], (gp / kVStages) & 1, abort)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint64_t vd = v_desc0 + ((st * kTile) >> 4);
+        const uint32_t pa = tmem + (gp & 1) * 128;   // P of tile gp: first 64 columns of its S buffer
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint64_t a = umma_desc_sw128(qa + (kk >> 2) * kSlab + (kk & 3) * 32, 16, 1024);
-              const uint64_t b = umma_desc_sw128(kb + (kk >> 2) * kSlab + (kk & 3) * 32, 16, 1024);
-              umma_bf16_ss(tmem + st * 128, a, b, idesc_qk, kk > 0);
-            }
-            umma_commit(&bars[B_SFULL + st]);
-            umma_commit(&bars[B_KEMPTY + st]);
-            if (j_q == nkv_q - 1) umma_commit(&bars[B_QEMPTY + qb]);
-          }
-          __syncwarp();
-          ++gq;
-          if (++j_q == nkv_q) {
-            j_q = 0;
-            nkv_q = -1;
-            ++it_q;
-          }
-          did = true;
-        }
+        for (int kk = 0; kk < 8; ++kk)   // V: 16 keys (2048 B) per step; P: 8 columns per step; fresh O per item
+          umma_bf16_ts(tmem + 256, pa + kk * 8, vd + kk * (2048 >> 4), idesc_pv, (j_p > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&bars[B_ODONE]);
+        umma_commit(&bars[B_VEMPTY + st]);
       }
-      if (gp < gq) {
-        if (nkv_p < 0) nkv_p = items[2 * (it_p % kItemRing)].w;   // published before QK of this item ran
-        const int st = gp & 1;
-        if (all_ready(&bars[B_PFULL], gp & 1) && all_ready(&bars[B_VFULL + st], (gp >> 1) & 1)) {
-          tc_fence_after();
-          if (lane == 0) {
-            const uint32_t vb = v_base + st * kTile;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint64_t a = umma_desc_sw128(p_base + (kk >> 2) * kSlab + (kk & 3) * 32, 16, 1024);
-              const uint64_t b = umma_desc_sw128(vb + kk * 2048, kSlab, 1024);
-              umma_bf16_ss(tmem + 256, a, b, idesc_pv, (j_p > 0 || kk > 0) ? 1u : 0u);   // fresh O per item
-            }
-            umma_commit(&bars[B_ODONE]);
-            umma_commit(&bars[B_VEMPTY + st]);
-          }
-          __syncwarp();
-          ++gp;
-          if (++j_p == nkv_p) {
-            j_p = 0;
-            nkv_p = -1;
-            ++it_p;
-          }
-          did = true;
-        }
+      __syncwarp();
+      ++gp;
+      if (++j_p == nkv_p) {
+        j_p = 0;
+        ++it_p;
       }
-      if (did) {
-        last_progress = globaltimer();
-      } else {
-        const bool timed_out = globaltimer() - last_progress > kWaitLimitNs;
-        if (__any_sync(kFull, *abort != 0 || timed_out)) {
-          if (lane == 0 && *abort == 0) {
-            *abort = 1;
-            atomicOr(&g_error_word, kErrTimeout);
-          }
-          __syncwarp();
-          break;
-        }
-        // nothing ready: sleep in hardware (at most 64 ns) on the next PV input, else on the next K tile
-        if (gp < gq) {
-          (void)mbar_try_wait_hint(&bars[B_PFULL], gp & 1, 64);
-        } else if (it_q < my_items) {
-          (void)mbar_try_wait_hint(&bars[B_KFULL + (gq & 1)], (gq >> 1) & 1, 64);
-        }
-        __syncwarp();
-      }
+      issue_qk();
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax + epilogue (thread = query row)
@@ -343,13 +325,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       const int lim = L - n + qt * 128 + t;   // this row sees keys <= lim
       float m_used = kNegInf, l = 0.f;
       for (int j = 0; j < nkv && alive; ++j, ++g) {
-        const int st = g & 1;
+        const int st = g & 1;              // S / P buffer
+        const int vs = g % kVStages;       // V ring slot
         // paged keys past the sequence end may be stale or uninitialised: zero V there (P is 0 there anyway)
         if (paged && j * 128 + 127 >= L) {
-          alive = mbar_wait_warp(&bars[B_VFULL + st], (g >> 1) & 1, abort);
+          alive = mbar_wait_warp(&bars[B_VFULL + vs], (g / kVStages) & 1, abort);
           if (!alive) break;
           if (j * 128 + t >= L) {
-            uint8_t* vrow = smem + kOffV + st * kTile + t * 128;
+            uint8_t* vrow = smem + kOffV + vs * kTile + t * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0u, 0u, 0u, 0u);
@@ -363,8 +346,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         float s[128];
 #pragma unroll
         for (int c = 0; c < 128; c += 32) tmem_ld32(t_lane + st * 128 + c, s + c);
-        tc_fence_before();
-        mbar_arrive(&bars[B_SEMPTY + st]);
         const int kmax = lim - j * 128;          // columns > kmax are masked for this row
         // row maximum with 8 independent partial maxima (one softmax warp per SM quarter: ILP hides latency)
         float m8[8];
@@ -384,13 +365,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
                                fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         const float m_cand = fmaxf(m_used, mx * p.scale_log2);
         const bool rescale = m_used != kNegInf && m_cand > m_used + kRescaleLog2;
-        // P buffer reuse and any O rescale both need the previous PV product complete
-        if (pv_seen < g) {
-          alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
-          if (!alive) break;
-          pv_seen = g;
-        }
         if (j > 0 && __any_sync(kFull, rescale)) {
+          // O must hold every earlier PV product of this item before it is rescaled
+          if (pv_seen < g) {
+            alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
+            if (!alive) break;
+            pv_seen = g;
+          }
           const float alpha = rescale ? fast_exp2(m_used - m_cand) : 1.f;
           tc_fence_after();
 #pragma unroll 1
@@ -406,50 +387,78 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         if (rescale || m_used == kNegInf) m_used = m_cand;
         const float neg_m = -m_used;
         float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        // P row t, 8 keys per 16-byte chunk: keys 0-63 in slab 0, 64-127 in slab 1, chunks swizzled by row
+        // P row t (bf16 pairs, lower half = even key) into columns 0..63 of this tile's S buffer
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          float pv[8];
+        for (int h = 0; h < 2; ++h) {
+          float pk[32];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float x = s[8 * c + i];
-            pv[i] = x == kNegInf ? 0.f : fast_exp2(fmaf(x, p.scale_log2, neg_m));
-            sum8[i] += pv[i];
+          for (int c = 0; c < 64; c += 2) {
+            const float x0 = s[64 * h + c], x1 = s[64 * h + c + 1];
+            const float p0 = x0 == kNegInf ? 0.f : fast_exp2(fmaf(x0, p.scale_log2, neg_m));
+            const float p1 = x1 == kNegInf ? 0.f : fast_exp2(fmaf(x1, p.scale_log2, neg_m));
+            sum8[c & 7] += p0;
+            sum8[(c + 1) & 7] += p1;
+            pk[c >> 1] = __uint_as_float(pack_bf16x2(p0, p1));
           }
-          const uint4 v = make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]), pack_bf16x2(pv[4], pv[5]),
-                                     pack_bf16x2(pv[6], pv[7]));
-          *reinterpret_cast<uint4*>(smem + kOffP + (c >> 3) * kSlab + sw128_offset(t, c & 7)) = v;
+          tmem_st32(t_lane + st * 128 + 32 * h, pk);
         }
         l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
-        fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&bars[B_PFULL]);
+        // keep the PV completions observed in order (never more than one behind)
+        if (pv_seen < g) {
+          alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
+          if (!alive) break;
+          pv_seen = g;
+        }
       }
       if (!alive) break;
-      // ---- epilogue: O / l for the tile's valid rows
+      // ---- epilogue: O / l for the tile's valid rows.  The item's Q buffer is idle now (its last S product ran
+      // before the last PV product): each warp stages its own 32 rows there (16-byte chunks swizzled by row), then
+      // writes whole 256-byte rows with coalesced stores, and the 128 threads release the buffer.
       alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
       if (!alive) break;
       pv_seen = g;
       tc_fence_after();
+      const int qb = it_count & 1;
+      uint8_t* stage = smem + kOffQ + qb * kTile;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = p.out + (int64_t)(q0 + qt * 128 + t) * p.out_row_stride + (int64_t)h * kHeadDim;
 #pragma unroll 1
       for (int c = 0; c < 128; c += 32) {
         float ot[32];
         tmem_ld32(t_lane + 256 + c, ot);
-        if (t < rows) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 v;
-            v.x = pack_bf16x2(ot[i] * inv, ot[i + 1] * inv);
-            v.y = pack_bf16x2(ot[i + 2] * inv, ot[i + 3] * inv);
-            v.z = pack_bf16x2(ot[i + 4] * inv, ot[i + 5] * inv);
-            v.w = pack_bf16x2(ot[i + 6] * inv, ot[i + 7] * inv);
-            *reinterpret_cast<uint4*>(dst + c + i) = v;
-          }
+        for (int i = 0; i < 32; i += 8) {
+          uint4 v;
+          v.x = pack_bf16x2(ot[i] * inv, ot[i + 1] * inv);
+          v.y = pack_bf16x2(ot[i + 2] * inv, ot[i + 3] * inv);
+          v.z = pack_bf16x2(ot[i + 4] * inv, ot[i + 5] * inv);
+          v.w = pack_bf16x2(ot[i + 6] * inv, ot[i + 7] * inv);
+          const int chunk = (c + i) >> 3;
+          *reinterpret_cast<uint4*>(stage + t * 256 + ((chunk ^ (t & 15)) << 4)) = v;
         }
       }
       tc_fence_before();
+      __syncwarp();
+      // rows 32*wq .. 32*wq+31, eight at a time with independent loads (whole 256-byte rows per store)
+#pragma unroll 1
+      for (int r0 = 32 * wq; r0 < 32 * wq + 32; r0 += 8) {
+        uint2 v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = r0 + i;
+          v[i] = *reinterpret_cast<const uint2*>(stage + r * 256 + ((((lane >> 1) ^ (r & 15)) << 4) | ((lane & 1) << 3)));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = r0 + i;
+          if (r < rows)
+            *reinterpret_cast<uint2*>(p.out + (int64_t)(q0 + qt * 128 + r) * p.out_row_stride +
+                                      (int64_t)h * kHeadDim + lane * 4) = v[i];
+        }
+      }
+      __syncwarp();
+      mbar_arrive(&bars[B_QEMPTY + qb]);
     }
   }
 
