@@ -12,8 +12,11 @@
 // are thread-local (no shuffles, no barriers between the softmax warps).  O is rescaled in TMEM only when a row's
 // maximum grows by more than 2^8 (until then P values up to 256 are exact enough in bf16 and FP32 sums).
 //
-// Warp roles (256 threads): 0 = Q + K producer (also publishes the item descriptors), 3 = V producer, 1 = TMEM owner
-// + UMMA issuer (polls, issues whichever product is ready), 2 = idle, 4..7 = softmax + epilogue.
+// Warp roles (384 threads): 0 = Q + K producer (also publishes the item descriptors), 3 = V producer, 1 = TMEM owner
+// + UMMA issuer, 2 = idle, 4..11 = softmax + epilogue in two warpgroups: thread (group w, row t) owns keys
+// [64w, 64w + 64) of query row t, so each S tile costs a thread 64 exponentials (a quarter of them on the FMA pipe
+// through exp2_poly) and two warps share each SM quarter to hide MUFU / TMEM latency.  The two halves of a row
+// exchange their maxima through shared memory and their sums through spare TMEM columns.
 #include "nva_ptx.cuh"
 #include "nva_kernels.h"
 
@@ -21,7 +24,7 @@ namespace nva {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;           // 4 service warps + 2 softmax warpgroups
 constexpr int kSlab = 128 * 128;       // 128 rows x 128 bytes
 constexpr int kTile = 2 * kSlab;       // 128 rows x 256 bytes (all 128 dims, or 128 keys of P)
 constexpr int kItemRing = 8;           // item descriptors: producer is at most ~5 items ahead of the softmax warps
@@ -37,9 +40,10 @@ constexpr int kOffK = kOffQ + 2 * kTile;              // K ring
 constexpr int kOffV = kOffK + kKStages * kTile;       // V ring
 constexpr int kOffBars = kOffV + kVStages * kTile;    // 32 x u64
 constexpr int kOffItems = kOffBars + 32 * 8;      // kItemRing x 2 x int4
-constexpr int kOffTmem = kOffItems + kItemRing * 32;
+constexpr int kOffRed = kOffItems + kItemRing * 32;   // [2 tiles][2 groups][128 rows] half-row maxima
+constexpr int kOffTmem = kOffRed + 2 * 2 * 128 * 4;
 constexpr int kOffAbort = kOffTmem + 4;
-constexpr int kSmemBytes = kOffAbort + 4 + 1024;
+constexpr int kSmemBytes = kOffAbort + 4;             // the dynamic shared memory base is 1024-aligned (checked)
 static_assert(kSmemBytes <= 232448, "prefill shared memory budget");
 
 enum {
@@ -138,10 +142,15 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(const PrefillParams 
 __global__ void __launch_bounds__(kThreads, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem_raw) & 1023u) != 0) {   // the swizzled layouts need a 1024-byte aligned base
+    if (threadIdx.x == 0) atomicOr(&g_error_word, kErrTimeout);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
   int4* items = reinterpret_cast<int4*>(smem + kOffItems);
+  float* red = reinterpret_cast<float*>(smem + kOffRed);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + kOffAbort);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -150,7 +159,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[B_QFULL + i], 1);
-      mbar_init(&bars[B_QEMPTY + i], 128);   // released by the softmax threads after the item's epilogue
+      mbar_init(&bars[B_QEMPTY + i], 256);   // released by the softmax threads after the item's epilogue
       mbar_init(&bars[B_KFULL + i], 1);
       mbar_init(&bars[B_KEMPTY + i], 1);
       mbar_init(&bars[B_SFULL + i], 1);
@@ -159,7 +168,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       mbar_init(&bars[B_VFULL + i], 1);
       mbar_init(&bars[B_VEMPTY + i], 1);
     }
-    mbar_init(&bars[B_PFULL], 128);
+    mbar_init(&bars[B_PFULL], 256);
     mbar_init(&bars[B_ODONE], 1);
     for (int i = 0; i < kItemRing; ++i) mbar_init(&bars[B_ITEM + i], 1);
     *abort = 0;
@@ -310,28 +319,36 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       issue_qk();
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------------------ softmax + epilogue (thread = query row)
-    const int t = tid - 128;
-    const int wq = t >> 5;
+    // ------------------------------------------------------------ softmax + epilogue: two warpgroups
+    // All eight softmax warps run the same sequence of named barriers (bar.red.or of "gave up"), one per tile and
+    // two per item, so they always leave together if a wait expires.
+    const int wg = (warp - 4) >> 2;           // key half: columns [64 wg, 64 wg + 64)
+    const int wq = warp & 3;                  // TMEM lane quadrant
+    const int t = wq * 32 + lane;             // query row within the tile
+    const int c0 = 64 * wg;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     int g = 0, pv_seen = 0, it_count = 0;
     bool alive = true;
-    for (int k = blockIdx.x; k < n_items && alive; k += gridDim.x, ++it_count) {
+    for (int k = blockIdx.x; k < n_items; k += gridDim.x, ++it_count) {
       const int e = it_count % kItemRing;
-      alive = mbar_wait_warp(&bars[B_ITEM + e], (it_count / kItemRing) & 1, abort);
-      if (!alive) break;
-      const int4 i0 = items[2 * e], i1 = items[2 * e + 1];
+      alive = alive && mbar_wait_warp(&bars[B_ITEM + e], (it_count / kItemRing) & 1, abort);
+      int4 i0 = make_int4(0, 0, 0, 1), i1 = make_int4(0, 0, 0, 0);
+      if (alive) {
+        i0 = items[2 * e];
+        i1 = items[2 * e + 1];
+      }
       const int h = i0.z, nkv = i0.w, n = i1.x, L = i1.y, q0 = i1.z, rows = i1.w, qt = i0.y;
       const int lim = L - n + qt * 128 + t;   // this row sees keys <= lim
-      float m_used = kNegInf, l = 0.f;
-      for (int j = 0; j < nkv && alive; ++j, ++g) {
+      float m_used = kNegInf, l = 0.f;       // l: this thread's half of the row sum
+      for (int j = 0; j < nkv; ++j, ++g) {
         const int st = g & 1;              // S / P buffer
         const int vs = g % kVStages;       // V ring slot
+        float s[64];
+        float mpart = kNegInf;
         // paged keys past the sequence end may be stale or uninitialised: zero V there (P is 0 there anyway)
-        if (paged && j * 128 + 127 >= L) {
+        if (alive && wg == 0 && paged && j * 128 + 127 >= L) {
           alive = mbar_wait_warp(&bars[B_VFULL + vs], (g / kVStages) & 1, abort);
-          if (!alive) break;
-          if (j * 128 + t >= L) {
+          if (alive && j * 128 + t >= L) {
             uint8_t* vrow = smem + kOffV + vs * kTile + t * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
@@ -340,93 +357,115 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
             }
           }
         }
-        alive = mbar_wait_warp(&bars[B_SFULL + st], (g >> 1) & 1, abort);
-        if (!alive) break;
-        tc_fence_after();
-        float s[128];
+        alive = alive && mbar_wait_warp(&bars[B_SFULL + st], (g >> 1) & 1, abort);
+        const int kmax = lim - j * 128 - c0;     // columns > kmax of this half are masked for this row
+        if (alive) {
+          tc_fence_after();
+          tmem_ld32(t_lane + st * 128 + c0, s);
+          tmem_ld32(t_lane + st * 128 + c0 + 32, s + 32);
+          float m8[8];
 #pragma unroll
-        for (int c = 0; c < 128; c += 32) tmem_ld32(t_lane + st * 128 + c, s + c);
-        const int kmax = lim - j * 128;          // columns > kmax are masked for this row
-        // row maximum with 8 independent partial maxima (one softmax warp per SM quarter: ILP hides latency)
-        float m8[8];
+          for (int i = 0; i < 8; ++i) m8[i] = kNegInf;
+          if (kmax >= 63) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = kNegInf;
-        if (kmax >= 127) {
+            for (int c = 0; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
+          } else {
 #pragma unroll
-          for (int c = 0; c < 128; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
-        } else {
-#pragma unroll
-          for (int c = 0; c < 128; ++c) {
-            s[c] = c <= kmax ? s[c] : kNegInf;
-            m8[c & 7] = fmaxf(m8[c & 7], s[c]);
+            for (int c = 0; c < 64; ++c) {
+              s[c] = c <= kmax ? s[c] : kNegInf;
+              m8[c & 7] = fmaxf(m8[c & 7], s[c]);
+            }
           }
+          mpart = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+          red[(st * 2 + wg) * 128 + t] = mpart;
         }
-        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        if (named_bar_any(1, 256, !alive)) {
+          alive = false;
+          break;
+        }
+        const float mx = fmaxf(mpart, red[(st * 2 + (wg ^ 1)) * 128 + t]);
         const float m_cand = fmaxf(m_used, mx * p.scale_log2);
         const bool rescale = m_used != kNegInf && m_cand > m_used + kRescaleLog2;
         if (j > 0 && __any_sync(kFull, rescale)) {
           // O must hold every earlier PV product of this item before it is rescaled
           if (pv_seen < g) {
             alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
-            if (!alive) break;
             pv_seen = g;
           }
-          const float alpha = rescale ? fast_exp2(m_used - m_cand) : 1.f;
-          tc_fence_after();
+          if (alive) {
+            const float alpha = rescale ? fast_exp2(m_used - m_cand) : 1.f;
+            tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < 128; c += 32) {
-            float ot[32];
-            tmem_ld32(t_lane + 256 + c, ot);
+            for (int c = 0; c < 64; c += 32) {
+              float ot[32];
+              tmem_ld32(t_lane + 256 + c0 + c, ot);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ot[i] *= alpha;
-            tmem_st32(t_lane + 256 + c, ot);
+              for (int i = 0; i < 32; ++i) ot[i] *= alpha;
+              tmem_st32(t_lane + 256 + c0 + c, ot);
+            }
+            if (rescale) l *= alpha;
           }
-          if (rescale) l *= alpha;
         }
         if (rescale || m_used == kNegInf) m_used = m_cand;
-        const float neg_m = -m_used;
-        float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        // P row t (bf16 pairs, lower half = even key) into columns 0..63 of this tile's S buffer
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        if (alive) {
+          const float neg_m = -m_used;
+          const float sc = p.scale_log2;
+          float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
           float pk[32];
+          const bool full = kmax >= 63;
 #pragma unroll
           for (int c = 0; c < 64; c += 2) {
-            const float x0 = s[64 * h + c], x1 = s[64 * h + c + 1];
-            const float p0 = x0 == kNegInf ? 0.f : fast_exp2(fmaf(x0, p.scale_log2, neg_m));
-            const float p1 = x1 == kNegInf ? 0.f : fast_exp2(fmaf(x1, p.scale_log2, neg_m));
+            float p0, p1;
+            if ((c & 7) == 6) {   // a quarter of the exponentials on the FMA pipe
+              p0 = exp2_poly(fmaf(s[c], sc, neg_m));
+              p1 = exp2_poly(fmaf(s[c + 1], sc, neg_m));
+            } else {
+              p0 = fast_exp2(fmaf(s[c], sc, neg_m));
+              p1 = fast_exp2(fmaf(s[c + 1], sc, neg_m));
+            }
+            if (!full) {
+              p0 = s[c] == kNegInf ? 0.f : p0;
+              p1 = s[c + 1] == kNegInf ? 0.f : p1;
+            }
             sum8[c & 7] += p0;
             sum8[(c + 1) & 7] += p1;
             pk[c >> 1] = __uint_as_float(pack_bf16x2(p0, p1));
           }
-          tmem_st32(t_lane + st * 128 + 32 * h, pk);
-        }
-        l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
-        tc_fence_before();
-        mbar_arrive(&bars[B_PFULL]);
-        // keep the PV completions observed in order (never more than one behind)
-        if (pv_seen < g) {
-          alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
-          if (!alive) break;
-          pv_seen = g;
+          // P (bf16 pairs, lower half = even key): keys [64 wg, 64 wg + 64) -> columns [32 wg, 32 wg + 32)
+          tmem_st32(t_lane + st * 128 + 32 * wg, pk);
+          l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+          tc_fence_before();
+          mbar_arrive(&bars[B_PFULL]);
+          // keep the PV completions observed in order (never more than one behind)
+          if (pv_seen < g) {
+            alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
+            pv_seen = g;
+          }
         }
       }
-      if (!alive) break;
-      // ---- epilogue: O / l for the tile's valid rows.  The item's Q buffer is idle now (its last S product ran
-      // before the last PV product): each warp stages its own 32 rows there (16-byte chunks swizzled by row), then
-      // writes whole 256-byte rows with coalesced stores, and the 128 threads release the buffer.
-      alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
-      if (!alive) break;
-      pv_seen = g;
+      // ---- epilogue: O / l for the tile's valid rows.  The two half-row sums meet in TMEM columns 384/385; O is
+      // staged in the item's idle Q buffer (its last S product ran before the last PV product), 16-byte chunks
+      // swizzled by row, then written back as whole 256-byte rows; the 256 threads then release the buffer.
+      if (alive) {
+        alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
+        pv_seen = g;
+        if (alive) {
+          tmem_st1(t_lane + 384 + wg, l);
+          tc_fence_before();
+        }
+      }
+      if (named_bar_any(1, 256, !alive)) break;
       tc_fence_after();
+      float lp[2];
+      tmem_ld2(t_lane + 384, lp);
+      const float lt = lp[0] + lp[1];
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
       const int qb = it_count & 1;
       uint8_t* stage = smem + kOffQ + qb * kTile;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
+      for (int c = 0; c < 64; c += 32) {
         float ot[32];
-        tmem_ld32(t_lane + 256 + c, ot);
+        tmem_ld32(t_lane + 256 + c0 + c, ot);
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
           uint4 v;
@@ -434,15 +473,16 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           v.y = pack_bf16x2(ot[i + 2] * inv, ot[i + 3] * inv);
           v.z = pack_bf16x2(ot[i + 4] * inv, ot[i + 5] * inv);
           v.w = pack_bf16x2(ot[i + 6] * inv, ot[i + 7] * inv);
-          const int chunk = (c + i) >> 3;
+          const int chunk = (c0 + c + i) >> 3;
           *reinterpret_cast<uint4*>(stage + t * 256 + ((chunk ^ (t & 15)) << 4)) = v;
         }
       }
       tc_fence_before();
-      __syncwarp();
-      // rows 32*wq .. 32*wq+31, eight at a time with independent loads (whole 256-byte rows per store)
+      if (named_bar_any(1, 256, false)) break;   // both halves of every row staged
+      // rows 16 w8 .. 16 w8 + 15 per softmax warp w8, eight at a time with independent loads
+      const int w8 = warp - 4;
 #pragma unroll 1
-      for (int r0 = 32 * wq; r0 < 32 * wq + 32; r0 += 8) {
+      for (int r0 = 16 * w8; r0 < 16 * w8 + 16; r0 += 8) {
         uint2 v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
