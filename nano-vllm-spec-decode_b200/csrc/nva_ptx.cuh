@@ -267,6 +267,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
+// True in exactly one lane of a converged warp (the lane elect.sync picks).  Single-thread tcgen05 / TMA issue
+// goes through an elected lane rather than a fixed lane behind a divergent branch: next to two busy softmax warps
+// on the same SM sub-partition, a 128x128x16 UMMA stream then runs at ~75-90 cycles per instruction instead of
+// ~120-190 (64 is the tensor pipe's own rate).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(e));
+  return e != 0;
+}
+
 // ---------------------------------------------------------------- tcgen05: UMMA
 // Shared-memory matrix descriptor (sm_100 format): start address, leading / stride byte offsets (all >> 4),
 // version 1 at bits [46,48), swizzle mode at bits [61,64) (2 = 128-byte swizzle).

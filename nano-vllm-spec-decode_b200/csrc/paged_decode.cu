@@ -336,7 +336,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           stop = true;
           break;
         }
-        if (lane == 0) {
+        if (elect_one()) {
           if (is_k) {
             const int e = jj % kInfoRing;
             info[2 * e] = make_int4(bi, gi, ji, fi);
@@ -352,7 +352,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       }
     }
   } else if (warp == 1 && ntiles > 0) {
-    // ------------------------------------------------------------ UMMA issuer (whole warp polls, lane 0 issues)
+    // ------------------------------------------------------------ UMMA issuer (whole warp polls, an elected lane issues)
     const uint64_t q_desc0 = umma_desc_sw128(smem_u32(smem + C::kQ), 16, 1024);
     const uint64_t k_desc0 = umma_desc_sw128(smem_u32(smem + C::kK), 16, 1024);
     const uint64_t v_desc0 = umma_desc_sw128(smem_u32(smem + C::kV), kSlab, 1024);
@@ -374,7 +374,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       const int buf = qk & 1;
       if (!mbar_wait_warp(&bars[B_SEMPTY + buf], ((qk >> 1) & 1) ^ 1, abort)) { ok = false; return; }
       tc_fence_after();
-      if (lane == 0) {
+      if (elect_one()) {
         // K-major SW128 operands: step k at +32 B within a 128-byte row, steps 4..7 in the second slab
         constexpr uint32_t kOffK[8] = {0, 2, 4, 6, kSlab >> 4, (kSlab >> 4) + 2, (kSlab >> 4) + 4, (kSlab >> 4) + 6};
         constexpr uint32_t kOffQ[8] = {0, 2, 4, 6, (NP * 128) >> 4, ((NP * 128) >> 4) + 2, ((NP * 128) >> 4) + 4,
@@ -398,7 +398,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       const uint32_t idesc_pv =
           umma_idesc_bf16(128, min(NP, mma_width(info[2 * (pv % kInfoRing) + 1].x * G)), true, true);
       tc_fence_after();
-      if (lane == 0) {
+      if (elect_one()) {
         // A = V^T: 16 tokens per step (two 8-row groups, SBO 1024; two 64-dim slabs, LBO 16 KB) -> +2048 B;
         // B = P^T: 16 tokens per step (two 8-token core-matrix groups, LBO 128; 8-row groups, SBO 2048) -> +256 B
         constexpr uint32_t kOffV[8] = {0, 128, 256, 384, 512, 640, 768, 896};

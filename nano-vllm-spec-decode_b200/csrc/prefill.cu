@@ -202,7 +202,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       const Item it = load_item(p, k, total);
       const int kvh = it.h / p.group;
       if (is_k) {
-        if (lane == 0) {
+        if (elect_one()) {
           const int e = it_count % kItemRing;
           items[2 * e] = make_int4(it.b, it.qt, it.h, it.nkv);
           items[2 * e + 1] = make_int4(it.n, it.L, it.q0, it.rows);
@@ -210,7 +210,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         }
         const int qb = it_count & 1;
         if (!mbar_wait_warp(&bars[B_QEMPTY + qb], ((it_count >> 1) & 1) ^ 1, abort)) break;
-        if (lane == 0) {
+        if (elect_one()) {
           mbar_arrive_expect_tx(&bars[B_QFULL + qb], kTile);
           uint8_t* dst = smem + kOffQ + qb * kTile;
           tma_load_3d(dst, &tm_q, 0, it.h, it.q0 + it.qt * 128, &bars[B_QFULL + qb]);
@@ -242,7 +242,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
             stop = true;
             break;
           }
-          if (lane == 0) {
+          if (elect_one()) {
             mbar_arrive_expect_tx(&full[st], kTile);
             tma_load_3d(ring + st * kTile, tm, 0, kvh, r0, &full[st]);
             tma_load_3d(ring + st * kTile + kSlab, tm, 64, kvh, r0, &full[st]);
@@ -278,7 +278,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       const int st = gq & 1;
       if (!mbar_wait_warp(&bars[B_KFULL + st], (gq >> 1) & 1, abort)) { ok = false; return; }
       tc_fence_after();
-      if (lane == 0) {
+      if (elect_one()) {
         // K-major SW128 operands: step k sits at +32 B within a 128-byte row, steps 4..7 in the second slab
         constexpr uint32_t kOff[8] = {0, 2, 4, 6, kSlab >> 4, (kSlab >> 4) + 2, (kSlab >> 4) + 4, (kSlab >> 4) + 6};
         umma_bf16_ss_x8(tmem + st * 128, q_desc0 + ((qb * kTile) >> 4), k_desc0 + ((st * kTile) >> 4), idesc_qk, 0u,
@@ -301,7 +301,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       if (!mbar_wait_warp(&bars[B_PFULL], gp & 1, abort)) break;
       if (!mbar_wait_warp(&bars[B_VFULL + st], (gp / kVStages) & 1, abort)) break;
       tc_fence_after();
-      if (lane == 0) {
+      if (elect_one()) {
         const uint64_t vd = v_desc0 + ((st * kTile) >> 4);
         const uint32_t pa = tmem + (gp & 1) * 128;   // P of tile gp: first 64 columns of its S buffer
 #pragma unroll
