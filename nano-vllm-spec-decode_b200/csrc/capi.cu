@@ -189,7 +189,8 @@ NVA_API int nva_paged_decode(const void* q, int64_t q_row_stride, const void* k_
 
 namespace {
 
-// Varlen workspace: the decode kernel's split partials (48-row tiles) followed by the prefill work plan.
+// Varlen workspace: the decode kernel's split partials (48-row tiles) followed by the prefill work plan
+// (count, capacity entries, work counter).
 size_t varlen_decode_part(int sms) { return (nva::decode_workspace_bytes(sms, 48) + 255) & ~size_t(255); }
 int varlen_plan_capacity(int32_t num_seqs, int32_t total_q) { return total_q / 128 + num_seqs + 1; }
 
@@ -203,7 +204,7 @@ NVA_API size_t nva_varlen_workspace_bytes(int32_t num_seqs, int32_t total_q, int
   if (num_kv_heads <= 0 || num_heads % num_kv_heads != 0 || num_seqs < 0 || total_q < 0) return 0;
   const int sms = sm_count();
   if (sms == 0) return 0;
-  return varlen_decode_part(sms) + sizeof(int32_t) * (1 + static_cast<size_t>(varlen_plan_capacity(num_seqs, total_q)));
+  return varlen_decode_part(sms) + sizeof(int32_t) * (2 + static_cast<size_t>(varlen_plan_capacity(num_seqs, total_q)));
 }
 
 NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void* key, int64_t key_row_stride,

@@ -63,7 +63,8 @@ struct PrefillParams {
   int32_t num_blocks;
   int32_t q_tiles_bound;        // capacity of the work plan: an upper bound on the number of 128-row q tiles
   float scale_log2;
-  int32_t* plan;                // workspace: [0] = number of q tiles, [1..] = (seq << 12 | q tile), heaviest first
+  int32_t* plan;                // workspace: [0] = number of q tiles, [1..] = (seq << 12 | q tile), heaviest first,
+                                // [1 + q_tiles_bound] = work counter (items taken after the first wave)
 };
 constexpr int kMaxPrefillTiles = 4096;
 cudaError_t launch_prefill(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,

@@ -2,8 +2,9 @@
 // for query runs longer than the decode kernel's 48-row tile: prefill chunks, with or without a paged prefix).
 //
 // Work item = (128-row query tile of one sequence, q head).  A one-CTA plan kernel lists the query tiles heaviest
-// first (most key tiles under the causal mask), and persistent CTAs take items round-robin from that list, so the
-// long diagonal tiles start first and the short ones fill the tail.
+// first (most key tiles under the causal mask); persistent CTAs take the first wave by block index and every later
+// item from an atomic counter (longest-processing-time-first list scheduling), so the long tiles start first and
+// the short ones fill in wherever a CTA frees up.
 //
 // Per item: S = Q K^T with M = 128 query rows on the TMEM lanes, N = 128 keys (A = Q, B = K tile, both K-major
 // 128B-swizzled straight from TMA); P = exp2(S * scale - m) in bf16, written back into the first 64 columns of its
@@ -135,7 +136,10 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(const PrefillParams 
     }
     p.plan[1 + rank] = code[i];
   }
-  if (tid == 0) p.plan[0] = total;
+  if (tid == 0) {
+    p.plan[0] = total;
+    p.plan[1 + p.q_tiles_bound] = 0;   // work counter of the main kernel
+  }
 }
 
 // ------------------------------------------------------------------------------------------------ main kernel
@@ -196,18 +200,41 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     uint64_t* full = bars + (is_k ? B_KFULL : B_VFULL);
     uint64_t* empty = bars + (is_k ? B_KEMPTY : B_VEMPTY);
     const int stages = is_k ? kKStages : kVStages;
-    int g = 0, it_count = 0;
+    int g = 0;
     bool stop = false;
-    for (int k = blockIdx.x; k < n_items && !stop; k += gridDim.x, ++it_count) {
-      const Item it = load_item(p, k, total);
-      const int kvh = it.h / p.group;
+    int* counter = p.plan + 1 + p.q_tiles_bound;
+    // The K producer takes each item and publishes it (nkv = 0: no more items) in the item ring; the V producer,
+    // the UMMA issuer and the softmax warps follow the ring.  The ring cannot overrun: the K producer waits for the
+    // Q buffer of item i - 2, whose epilogue comes after every consumer has read entry i - 2.
+    for (int it_count = 0; !stop; ++it_count) {
+      const int e = it_count % kItemRing;
+      Item it;
       if (is_k) {
+        int k = blockIdx.x;
+        if (it_count > 0) {
+          int v = 0;
+          if (elect_one()) v = atomicAdd(counter, 1);
+          k = gridDim.x + __reduce_add_sync(kFull, v);
+        }
+        it = load_item(p, k, total);   // invalid once k >= n_items
         if (elect_one()) {
-          const int e = it_count % kItemRing;
-          items[2 * e] = make_int4(it.b, it.qt, it.h, it.nkv);
-          items[2 * e + 1] = make_int4(it.n, it.L, it.q0, it.rows);
+          items[2 * e] = it.valid ? make_int4(it.b, it.qt, it.h, it.nkv) : make_int4(0, 0, 0, 0);
+          items[2 * e + 1] = it.valid ? make_int4(it.n, it.L, it.q0, it.rows) : make_int4(0, 0, 0, 0);
           mbar_arrive(&bars[B_ITEM + e]);
         }
+        __syncwarp();
+        if (!it.valid) break;
+      } else {
+        if (!mbar_wait_warp(&bars[B_ITEM + e], (it_count / kItemRing) & 1, abort)) break;
+        const int4 i0 = items[2 * e];
+        if (i0.w == 0) break;
+        it.b = i0.x;
+        it.h = i0.z;
+        it.nkv = i0.w;
+        it.k0 = paged ? 0 : __ldg(p.cu_k + it.b);
+      }
+      const int kvh = it.h / p.group;
+      if (is_k) {
         const int qb = it_count & 1;
         if (!mbar_wait_warp(&bars[B_QEMPTY + qb], ((it_count >> 1) & 1) ^ 1, abort)) break;
         if (elect_one()) {
@@ -262,17 +289,20 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     // Issue order: QK(0), QK(1), then PV(g), QK(g+2), ...  QK(g+2) overwrites the S buffer that holds P(g), so it
     // must follow PV(g) (the tensor pipe runs one thread's products in issue order); every wait is a blocking,
     // hardware-suspended mbarrier wait.  Tile indices g run across the CTA's items.
-    const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     int it_q = 0, j_q = 0, nkv_q = 0, gq = 0;   // next S product
     int it_p = 0, j_p = 0, gp = 0;              // next PV product
-    bool ok = true;
+    bool ok = true, q_done = false;             // q_done: the item ring's end marker was read (it_q items)
     auto issue_qk = [&]() {
-      if (!ok || it_q >= my_items) return;
+      if (!ok || q_done) return;
       const int qb = it_q & 1;
       if (j_q == 0) {
         const int e = it_q % kItemRing;
         if (!mbar_wait_warp(&bars[B_ITEM + e], (it_q / kItemRing) & 1, abort)) { ok = false; return; }
         nkv_q = items[2 * e].w;
+        if (nkv_q == 0) {
+          q_done = true;
+          return;
+        }
         if (!mbar_wait_warp(&bars[B_QFULL + qb], (it_q >> 1) & 1, abort)) { ok = false; return; }
       }
       const int st = gq & 1;
@@ -295,7 +325,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     };
     issue_qk();
     issue_qk();
-    while (ok && it_p < my_items) {
+    // S runs two tiles ahead of PV, so the end marker is read before PV reaches the last item
+    while (ok && (!q_done || it_p < it_q)) {
       const int nkv_p = items[2 * (it_p % kItemRing)].w;   // published (and awaited) before this item's first QK
       const int st = gp % kVStages;
       if (!mbar_wait_warp(&bars[B_PFULL], gp & 1, abort)) break;
@@ -321,7 +352,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax + epilogue: two warpgroups
     // All eight softmax warps run the same sequence of named barriers (bar.red.or of "gave up"), one per tile and
-    // two per item, so they always leave together if a wait expires.
+    // three per item, so they always leave together if a wait expires.
     const int wg = (warp - 4) >> 2;           // key half: columns [64 wg, 64 wg + 64)
     const int wq = warp & 3;                  // TMEM lane quadrant
     const int t = wq * 32 + lane;             // query row within the tile
@@ -329,7 +360,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     int g = 0, pv_seen = 0, it_count = 0;
     bool alive = true;
-    for (int k = blockIdx.x; k < n_items; k += gridDim.x, ++it_count) {
+    for (;; ++it_count) {
       const int e = it_count % kItemRing;
       alive = alive && mbar_wait_warp(&bars[B_ITEM + e], (it_count / kItemRing) & 1, abort);
       int4 i0 = make_int4(0, 0, 0, 1), i1 = make_int4(0, 0, 0, 0);
@@ -337,6 +368,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         i0 = items[2 * e];
         i1 = items[2 * e + 1];
       }
+      if (named_bar_any(1, 256, !alive || i0.w == 0)) break;   // end marker (or a wait gave up): all leave
       const int h = i0.z, nkv = i0.w, n = i1.x, L = i1.y, q0 = i1.z, rows = i1.w, qt = i0.y;
       const int lim = L - n + qt * 128 + t;   // this row sees keys <= lim
       float m_used = kNegInf, l = 0.f;       // l: this thread's half of the row sum
