@@ -393,22 +393,17 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const int kmax = lim - j * 128 - c0;     // columns > kmax of this half are masked for this row
         if (alive) {
           tc_fence_after();
-          tmem_ld32(t_lane + st * 128 + c0, s);
-          tmem_ld32(t_lane + st * 128 + c0 + 32, s + 32);
+          tmem_ld64(t_lane + st * 128 + c0, s);
+          if (kmax < 63) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) s[c] = c <= kmax ? s[c] : kNegInf;
+          }
           float m8[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = kNegInf;
-          if (kmax >= 63) {
-#pragma unroll
-            for (int c = 0; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
-          } else {
-#pragma unroll
-            for (int c = 0; c < 64; ++c) {
-              s[c] = c <= kmax ? s[c] : kNegInf;
-              m8[c & 7] = fmaxf(m8[c & 7], s[c]);
-            }
-          }
-          mpart = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+          for (int i = 0; i < 8; ++i)
+            m8[i] = fmaxf(fmax3(fmax3(s[i], s[i + 8], s[i + 16]), s[i + 24], s[i + 32]),
+                          fmax3(s[i + 40], s[i + 48], s[i + 56]));
+          mpart = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
           red[(st * 2 + wg) * 128 + t] = mpart;
         }
         if (named_bar_any(1, 256, !alive)) {
@@ -440,32 +435,34 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         }
         if (rescale || m_used == kNegInf) m_used = m_cand;
         if (alive) {
-          const float neg_m = -m_used;
-          const float sc = p.scale_log2;
-          float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          // masked keys hold -inf, so their MUFU weights are exp2(-inf) = 0; a row that has seen no key yet
+          // (m_used = -inf) subtracts 0 and gets only zeros
+          const float neg_m = m_used == kNegInf ? 0.f : -m_used;
+          const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(neg_m, neg_m);
+          float2 sum4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                            make_float2(0.f, 0.f)};
           float pk[32];
           const bool full = kmax >= 63;
 #pragma unroll
           for (int c = 0; c < 64; c += 2) {
-            float p0, p1;
-            if ((c & 7) == 6) {   // a quarter of the exponentials on the FMA pipe
-              p0 = exp2_poly(fmaf(s[c], sc, neg_m));
-              p1 = exp2_poly(fmaf(s[c + 1], sc, neg_m));
+            const float2 x = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
+            float2 pp;
+            if ((c & 7) == 6) {   // a quarter of the exponentials on the FMA pipe (2^-126 at -inf: zero them)
+              pp = exp2_poly2(x);
+              if (!full) {
+                pp.x = c <= kmax ? pp.x : 0.f;
+                pp.y = c + 1 <= kmax ? pp.y : 0.f;
+              }
             } else {
-              p0 = fast_exp2(fmaf(s[c], sc, neg_m));
-              p1 = fast_exp2(fmaf(s[c + 1], sc, neg_m));
+              pp = make_float2(fast_exp2(x.x), fast_exp2(x.y));
             }
-            if (!full) {
-              p0 = s[c] == kNegInf ? 0.f : p0;
-              p1 = s[c + 1] == kNegInf ? 0.f : p1;
-            }
-            sum8[c & 7] += p0;
-            sum8[(c + 1) & 7] += p1;
-            pk[c >> 1] = __uint_as_float(pack_bf16x2(p0, p1));
+            sum4[(c >> 1) & 3] = fadd2(sum4[(c >> 1) & 3], pp);
+            pk[c >> 1] = __uint_as_float(pack_bf16x2(pp.x, pp.y));
           }
           // P (bf16 pairs, lower half = even key): keys [64 wg, 64 wg + 64) -> columns [32 wg, 32 wg + 32)
           tmem_st32(t_lane + st * 128 + 32 * wg, pk);
-          l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+          const float2 s01 = fadd2(fadd2(sum4[0], sum4[1]), fadd2(sum4[2], sum4[3]));
+          l += s01.x + s01.y;
           tc_fence_before();
           mbar_arrive(&bars[B_PFULL]);
           // keep the PV completions observed in order (never more than one behind)
