@@ -249,7 +249,7 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
   const int max_n = np / group;                // query runs up to this length use the decode kernel
   const int cap = varlen_plan_capacity(num_seqs, total_q);
   if (cap > nva::kMaxPrefillTiles) return NVA_ERR_UNSUPPORTED;
-  const size_t need = varlen_decode_part(grid) + sizeof(int32_t) * (1 + static_cast<size_t>(cap));
+  const size_t need = varlen_decode_part(grid) + sizeof(int32_t) * (2 + static_cast<size_t>(cap));
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return NVA_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (paged) {
@@ -278,8 +278,11 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
     if (e != cudaSuccess) return cuda_fail(e);
   }
   if (!paged || max_seqlen_q > max_n) {
-    CUtensorMap tm_q;
+    CUtensorMap tm_q, tm_o;
     if ((rc = encode_rows(&tm_q, q, num_heads, total_q, q_row_stride * 2)) != NVA_OK) return rc;
+    // full 128-row output tiles leave through TMA stores when the output rows allow a tensor map
+    const bool o_tma = aligned16(out) && (out_row_stride * 2) % 16 == 0;
+    if (o_tma && (rc = encode_rows(&tm_o, out, num_heads, total_q, out_row_stride * 2)) != NVA_OK) return rc;
     nva::PrefillParams pp{};
     pp.q = static_cast<const __nv_bfloat16*>(q);
     pp.q_row_stride = q_row_stride;
@@ -297,10 +300,11 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
     pp.block_size = block_size;
     pp.num_blocks = num_blocks;
     pp.q_tiles_bound = cap;
+    pp.o_tma = o_tma ? 1 : 0;
     pp.scale_log2 = softmax_scale * 1.4426950408889634f;
     pp.plan = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + varlen_decode_part(grid));
     const int pgrid = static_cast<int>(std::min<int64_t>(grid, static_cast<int64_t>(cap) * num_heads));
-    cudaError_t e = nva::launch_prefill(tm_q, tm_k, tm_v, pp, pgrid, s);
+    cudaError_t e = nva::launch_prefill(tm_q, tm_k, tm_v, o_tma ? tm_o : tm_q, pp, pgrid, s);
     if (e != cudaSuccess) return cuda_fail(e);
   }
   return NVA_OK;

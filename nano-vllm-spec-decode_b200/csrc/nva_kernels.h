@@ -62,13 +62,14 @@ struct PrefillParams {
   int32_t block_size;
   int32_t num_blocks;
   int32_t q_tiles_bound;        // capacity of the work plan: an upper bound on the number of 128-row q tiles
+  int32_t o_tma;                // 1: full output tiles are written by TMA stores through the output tensor map
   float scale_log2;
   int32_t* plan;                // workspace: [0] = number of q tiles, [1..] = (seq << 12 | q tile), heaviest first,
                                 // [1 + q_tiles_bound] = work counter (items taken after the first wave)
 };
 constexpr int kMaxPrefillTiles = 4096;
 cudaError_t launch_prefill(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                           const PrefillParams& p, int grid, cudaStream_t stream);
+                           const CUtensorMap& tm_o, const PrefillParams& p, int grid, cudaStream_t stream);
 
 cudaError_t launch_store_kvcache(const void* key, int64_t key_row_stride, const void* value,
                                  int64_t value_row_stride, void* k_cache, void* v_cache, int64_t num_slots,

@@ -14,10 +14,12 @@
 // maximum grows by more than 2^8 (until then P values up to 256 are exact enough in bf16 and FP32 sums).
 //
 // Warp roles (384 threads): 0 = Q + K producer (also publishes the item descriptors), 3 = V producer, 1 = TMEM owner
-// + UMMA issuer, 2 = idle, 4..11 = softmax + epilogue in two warpgroups: thread (group w, row t) owns keys
+// + UMMA issuer, 2 = output writer, 4..11 = softmax + epilogue in two warpgroups: thread (group w, row t) owns keys
 // [64w, 64w + 64) of query row t, so each S tile costs a thread 64 exponentials (a quarter of them on the FMA pipe
-// through exp2_poly) and two warps share each SM quarter to hide MUFU / TMEM latency.  The two halves of a row
-// exchange their maxima through shared memory and their sums through spare TMEM columns.
+// through exp2_poly2) and two warps share each SM quarter to hide MUFU / TMEM latency.  The two halves of a row
+// exchange their maxima through shared memory and their sums through spare TMEM columns.  The softmax warps stage
+// the normalised O tile in the item's Q buffer (TMA's 128-byte-swizzled two-slab layout) and move on; the writer
+// warp stores it (TMA for full 128-row tiles, plain stores for a sequence's last partial tile) and frees the buffer.
 #include "nva_ptx.cuh"
 #include "nva_kernels.h"
 
@@ -49,7 +51,8 @@ static_assert(kSmemBytes <= 232448, "prefill shared memory budget");
 
 enum {
   B_QFULL = 0, B_QEMPTY = 2, B_KFULL = 4, B_KEMPTY = 6, B_VFULL = 8, B_VEMPTY = 11, B_SFULL = 14, B_PFULL = 16,
-  B_ODONE = 17, B_ITEM = 18   // B_ITEM + kItemRing <= 32
+  B_ODONE = 17, B_ITEM = 18,  // B_ITEM + kItemRing <= B_OSTAGED
+  B_OSTAGED = 26              // 2: normalised O of the item staged in Q buffer 0 / 1
 };
 
 struct Item {
@@ -79,10 +82,6 @@ __device__ __forceinline__ Item load_item(const PrefillParams& p, int k, int tot
   // uniform when no key is visible (those rows get a zero output)
   it.nkv = max(1, (it.L - it.n + last_row) / 128 + 1);
   return it;
-}
-
-__device__ __forceinline__ bool all_ready(uint64_t* bar, uint32_t parity) {
-  return __all_sync(kFull, mbar_test_wait(bar, parity));
 }
 
 // ------------------------------------------------------------------------------------------------ plan kernel
@@ -145,7 +144,8 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(const PrefillParams 
 // ------------------------------------------------------------------------------------------------ main kernel
 __global__ void __launch_bounds__(kThreads, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-               const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
+               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+               const PrefillParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
   if ((smem_u32(smem_raw) & 1023u) != 0) {   // the swizzled layouts need a 1024-byte aligned base
@@ -163,7 +163,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[B_QFULL + i], 1);
-      mbar_init(&bars[B_QEMPTY + i], 256);   // released by the softmax threads after the item's epilogue
+      mbar_init(&bars[B_QEMPTY + i], 1);     // released by the writer warp once the staged O has been read
+      mbar_init(&bars[B_OSTAGED + i], 256);  // the softmax threads' halves of O staged
       mbar_init(&bars[B_KFULL + i], 1);
       mbar_init(&bars[B_KEMPTY + i], 1);
       mbar_init(&bars[B_SFULL + i], 1);
@@ -181,6 +182,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
+    if (p.o_tma) tma_prefetch_desc(&tm_o);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -190,7 +192,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int total = p.plan[0];
-  const int n_items = total * p.num_heads;
 
   if (warp == 0 || warp == 3) {
     // ------------------------------------------------------------ Q+K (warp 0) and V (warp 3) producers
@@ -216,7 +217,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           if (elect_one()) v = atomicAdd(counter, 1);
           k = gridDim.x + __reduce_add_sync(kFull, v);
         }
-        it = load_item(p, k, total);   // invalid once k >= n_items
+        it = load_item(p, k, total);   // invalid once k >= number of tiles x heads
         if (elect_one()) {
           items[2 * e] = it.valid ? make_int4(it.b, it.qt, it.h, it.nkv) : make_int4(0, 0, 0, 0);
           items[2 * e + 1] = it.valid ? make_int4(it.n, it.L, it.q0, it.rows) : make_int4(0, 0, 0, 0);
@@ -349,10 +350,55 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       }
       issue_qk();
     }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ output writer
+    for (int it_count = 0;; ++it_count) {
+      const int e = it_count % kItemRing;
+      if (!mbar_wait_warp(&bars[B_ITEM + e], (it_count / kItemRing) & 1, abort)) break;
+      const int4 i0 = items[2 * e], i1 = items[2 * e + 1];
+      if (i0.w == 0) break;
+      const int qb = it_count & 1;
+      if (!mbar_wait_warp(&bars[B_OSTAGED + qb], (it_count >> 1) & 1, abort)) break;
+      const int h = i0.z, row0 = i1.z + i0.y * 128, rows = i1.w;
+      const uint8_t* stage = smem + kOffQ + qb * kTile;
+      if (p.o_tma && rows == 128) {
+        if (elect_one()) {
+          tma_store_3d(&tm_o, stage, 0, h, row0);
+          tma_store_3d(&tm_o, stage + kSlab, 64, h, row0);
+          tma_store_commit_wait_read();
+          mbar_arrive(&bars[B_QEMPTY + qb]);
+        }
+        __syncwarp();
+      } else {
+        // lane: 8 bytes (dims 4 lane .. 4 lane + 3) of each row, i.e. 16-byte chunk lane / 2 of the 256-byte row
+        const int chunk = lane >> 1;
+        const int off = (chunk >> 3) * kSlab + ((lane & 1) << 3);
+#pragma unroll 1
+        for (int r0 = 0; r0 < rows; r0 += 8) {
+          uint2 v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = r0 + i;
+            v[i] = *reinterpret_cast<const uint2*>(stage + off + r * 128 + (((chunk & 7) ^ (r & 7)) << 4));
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = r0 + i;
+            if (r < rows)
+              *reinterpret_cast<uint2*>(p.out + (int64_t)(row0 + r) * p.out_row_stride + (int64_t)h * kHeadDim +
+                                        lane * 4) = v[i];
+          }
+        }
+        fence_proxy_async_smem();   // these generic reads before the next TMA write into the buffer
+        __syncwarp();
+        if (elect_one()) mbar_arrive(&bars[B_QEMPTY + qb]);
+      }
+    }
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // every TMA store of this warp complete
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax + epilogue: two warpgroups
     // All eight softmax warps run the same sequence of named barriers (bar.red.or of "gave up"), one per tile and
-    // three per item, so they always leave together if a wait expires.
+    // two per item, so they always leave together if a wait expires.
     const int wg = (warp - 4) >> 2;           // key half: columns [64 wg, 64 wg + 64)
     const int wq = warp & 3;                  // TMEM lane quadrant
     const int t = wq * 32 + lane;             // query row within the tile
@@ -369,7 +415,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         i1 = items[2 * e + 1];
       }
       if (named_bar_any(1, 256, !alive || i0.w == 0)) break;   // end marker (or a wait gave up): all leave
-      const int h = i0.z, nkv = i0.w, n = i1.x, L = i1.y, q0 = i1.z, rows = i1.w, qt = i0.y;
+      const int nkv = i0.w, n = i1.x, L = i1.y, qt = i0.y;
       const int lim = L - n + qt * 128 + t;   // this row sees keys <= lim
       float m_used = kNegInf, l = 0.f;       // l: this thread's half of the row sum
       for (int j = 0; j < nkv; ++j, ++g) {
@@ -472,9 +518,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           }
         }
       }
-      // ---- epilogue: O / l for the tile's valid rows.  The two half-row sums meet in TMEM columns 384/385; O is
-      // staged in the item's idle Q buffer (its last S product ran before the last PV product), 16-byte chunks
-      // swizzled by row, then written back as whole 256-byte rows; the 256 threads then release the buffer.
+      // ---- epilogue: O / l.  The two half-row sums meet in TMEM columns 384/385; O is staged in the item's idle
+      // Q buffer (its last S product ran before the last PV product) in TMA's layout: dims [0, 64) and [64, 128) in
+      // two 128-row slabs, 16-byte chunk k of row r at slot k ^ (r & 7); the writer warp takes it from there.
       if (alive) {
         alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
         pv_seen = g;
@@ -502,32 +548,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           v.y = pack_bf16x2(ot[i + 2] * inv, ot[i + 3] * inv);
           v.z = pack_bf16x2(ot[i + 4] * inv, ot[i + 5] * inv);
           v.w = pack_bf16x2(ot[i + 6] * inv, ot[i + 7] * inv);
-          const int chunk = (c0 + c + i) >> 3;
-          *reinterpret_cast<uint4*>(stage + t * 256 + ((chunk ^ (t & 15)) << 4)) = v;
+          const int chunk = (c0 + c + i) >> 3;   // 16-byte chunk of the 256-byte row
+          *reinterpret_cast<uint4*>(stage + (chunk >> 3) * kSlab + t * 128 + (((chunk & 7) ^ (t & 7)) << 4)) = v;
         }
       }
       tc_fence_before();
-      if (named_bar_any(1, 256, false)) break;   // both halves of every row staged
-      // rows 16 w8 .. 16 w8 + 15 per softmax warp w8, eight at a time with independent loads
-      const int w8 = warp - 4;
-#pragma unroll 1
-      for (int r0 = 16 * w8; r0 < 16 * w8 + 16; r0 += 8) {
-        uint2 v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = r0 + i;
-          v[i] = *reinterpret_cast<const uint2*>(stage + r * 256 + ((((lane >> 1) ^ (r & 15)) << 4) | ((lane & 1) << 3)));
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = r0 + i;
-          if (r < rows)
-            *reinterpret_cast<uint2*>(p.out + (int64_t)(q0 + qt * 128 + r) * p.out_row_stride +
-                                      (int64_t)h * kHeadDim + lane * 4) = v[i];
-        }
-      }
-      __syncwarp();
-      mbar_arrive(&bars[B_QEMPTY + qb]);
+      fence_proxy_async_smem();   // staged rows visible to the writer's TMA store
+      mbar_arrive(&bars[B_OSTAGED + qb]);
     }
   }
 
@@ -546,14 +573,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
 }  // namespace
 
 cudaError_t launch_prefill(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
-                           const PrefillParams& p, int grid, cudaStream_t stream) {
+                           const CUtensorMap& tm_o, const PrefillParams& p, int grid, cudaStream_t stream) {
   if (p.num_seqs > kMaxDecodeSeqs || p.q_tiles_bound > kMaxPrefillTiles) return cudaErrorInvalidValue;
   prefill_plan_kernel<<<1, 1024, 0, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
-  prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, p);
+  prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, tm_o, p);
   return cudaGetLastError();
 }
 
