@@ -15,13 +15,14 @@
 // The split depends only on the batch's lengths (padding sequences of length 0 change nothing), and there is no
 // host value or device read-back involved: graph-capturable with a fixed launch geometry.
 //
-// Warp roles (256 threads):
+// Warp roles (256 threads; 384 for the 32/48-row instantiations):
 //   0 = K producer, 3 = V producer: block-table ids prefetched 32 tiles at a time, then TMA 64 dims x 128 tokens
 //       boxes into 3-stage rings; K slots are released right after S = K Q^T, V slots after the PV product;
 //   1 = TMEM owner + UMMA issuer: polls the ring / softmax barriers and issues whichever product is ready;
 //   2 = Q loader: gathers a segment's rows into the swizzled operand layout (cp.async, zero-filled padding);
-//   4..7 = softmax: thread ct owns TMEM lane ct (token ct of S^T, dim ct of O^T).  Column maxima and sums over
-//       the 128 tokens use a transposed butterfly (each shuffle stage halves the rows a lane carries).
+//   4..7 (and 8..11) = softmax: thread ct of a warpgroup owns TMEM lane ct (token ct of S^T, dim ct of O^T).
+//       Column maxima and sums over the 128 tokens use a transposed butterfly (each shuffle stage halves the rows
+//       a lane carries).  With two warpgroups each takes half of the rows; rows never interact in the softmax.
 #include <type_traits>
 
 #include "nva_ptx.cuh"
@@ -34,7 +35,6 @@ namespace {
 constexpr int kStages = 3;
 constexpr int kSlab = 128 * 128;        // 128 rows x 128 bytes (64 bf16 dims)
 constexpr int kTileBytes = 2 * kSlab;   // one K or V tile: dims 0-63 and 64-127
-constexpr int kThreads = 256;
 constexpr int kConsumerBase = 128;
 constexpr float kNegInf = -__builtin_huge_valf();
 constexpr uint32_t kFull = 0xffffffffu;
@@ -45,6 +45,9 @@ constexpr int kInfoRing = 8;
 
 template <int NP>
 struct Cfg {
+  static constexpr int kWG = NP >= 32 ? 2 : 1;                   // softmax warpgroups (row halves)
+  static constexpr int kThreads = kConsumerBase + 128 * kWG;
+  static constexpr int kRowsPerGroup = NP / kWG;                 // per-thread row arrays
   static constexpr int kQBuf = NP <= 32 ? 2 : 1;                 // Q double-buffered when shared memory allows
   static constexpr int kK = 0;                                   // K ring
   static constexpr int kV = kStages * kTileBytes;                // V ring
@@ -58,8 +61,8 @@ struct Cfg {
   static constexpr int kLred = kAlpha + 2 * NP * 4;              // [4][NP] column sums per warp
   static constexpr int kTmem = kLred + 4 * NP * 4;
   static constexpr int kAbort = kTmem + 4;
-  static constexpr int kScan = kAbort + 4;                       // [8]
-  static constexpr int kPrefix = kScan + 32;                     // [kMaxDecodeSeqs + 1]
+  static constexpr int kScan = kAbort + 4;                       // [16] per-warp prefix totals
+  static constexpr int kPrefix = kScan + 64;                     // [kMaxDecodeSeqs + 1]
   static constexpr int kEnd = kPrefix + (kMaxDecodeSeqs + 1) * 4;
   static constexpr int kBytes = kEnd + 1024;                     // + slack for 1024-byte alignment
 };
@@ -185,7 +188,7 @@ __device__ __forceinline__ void column_reduce(float* v, float* dst, int lane) {
   if ((lane & (kRep - 1)) == 0) dst[lane / kRep] = v[0];
 }
 
-// Column reduction of NR (8, 16, 32 or 48) values per thread within one warp into dst[0..NR).
+// Column reduction of NR (8, 16, 24, 32 or 48) values per thread within one warp into dst[0..NR).
 template <int NR, bool kMax>
 __device__ __forceinline__ void warp_columns(const float* x, float* dst, int lane) {
   float v[32];
@@ -193,6 +196,13 @@ __device__ __forceinline__ void warp_columns(const float* x, float* dst, int lan
 #pragma unroll
     for (int i = 0; i < NR; ++i) v[i] = x[i];
     column_reduce<NR, kMax>(v, dst, lane);
+  } else if constexpr (NR == 24) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = x[i];
+    column_reduce<16, kMax>(v, dst, lane);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = x[16 + i];
+    column_reduce<8, kMax>(v, dst + 16, lane);
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = x[i];
@@ -224,12 +234,40 @@ __device__ __forceinline__ void with_rows(int nr, F&& f) {
   }
 }
 
-__device__ __forceinline__ bool all_ready(uint64_t* bar, uint32_t parity) {
-  return __all_sync(kFull, mbar_test_wait(bar, parity));
+// The UMMA issuing lane, by row tile (measured on B200 against a softmax warp on the issuer's SM sub-partition):
+// elect.sync for 32/48-row tiles (verify k = 8 about 6% faster), a fixed lane 0 for the 16-row decode tile (about
+// 2% faster there).
+template <int NP>
+__device__ __forceinline__ bool umma_lane(int lane) {
+  if constexpr (NP >= 32) {
+    return elect_one();
+  } else {
+    return lane == 0;
+  }
+}
+
+// Rows a softmax warpgroup carries for an NR-wide tile: all of them with one group; with two, half (at least one
+// 8-row P^T vector each, so an 8-row tile gives the second group 8 padding rows).
+template <int NP, int NR>
+__device__ __forceinline__ constexpr int group_rows() {
+  return Cfg<NP>::kWG == 1 ? NR : (NR < 16 ? 8 : NR / 2);
+}
+
+// HR consecutive TMEM columns (8, 16 or 24) of this warp's lanes, one wait.
+template <int HR>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
+  if constexpr (HR == 8) {
+    tmem_ld8(taddr, v);
+  } else if constexpr (HR == 16) {
+    tmem_ld16(taddr, v);
+  } else {
+    static_assert(HR == 24, "row group width");
+    tmem_ld24(taddr, v);
+  }
 }
 
 template <int NP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<NP>::kThreads, 1)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const DecodeParams p) {
   using C = Cfg<NP>;
@@ -261,11 +299,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[B_SFULL + i], 1);
-      mbar_init(&bars[B_SEMPTY + i], 128);
+      mbar_init(&bars[B_SEMPTY + i], 128 * C::kWG);
       mbar_init(&bars[B_QFULL + i], 32);
       mbar_init(&bars[B_QEMPTY + i], 1);
     }
-    mbar_init(&bars[B_PFULL], 128);
+    mbar_init(&bars[B_PFULL], 128 * C::kWG);
     mbar_init(&bars[B_OFULL], 1);
     for (int i = 0; i < kInfoRing; ++i) mbar_init(&bars[B_INFO + i], 1);
     *abort = 0;
@@ -278,7 +316,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
-  build_prefix(p, prefix, warp_tot, tid, kThreads);   // ends with __syncthreads
+  build_prefix(p, prefix, warp_tot, tid, C::kThreads);   // ends with __syncthreads
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // let the combine kernel (launched as a programmatic dependent) get resident and run its prologue now; it waits
@@ -374,7 +412,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       const int buf = qk & 1;
       if (!mbar_wait_warp(&bars[B_SEMPTY + buf], ((qk >> 1) & 1) ^ 1, abort)) { ok = false; return; }
       tc_fence_after();
-      if (elect_one()) {
+      if (umma_lane<NP>(lane)) {
         // K-major SW128 operands: step k at +32 B within a 128-byte row, steps 4..7 in the second slab
         constexpr uint32_t kOffK[8] = {0, 2, 4, 6, kSlab >> 4, (kSlab >> 4) + 2, (kSlab >> 4) + 4, (kSlab >> 4) + 6};
         constexpr uint32_t kOffQ[8] = {0, 2, 4, 6, (NP * 128) >> 4, ((NP * 128) >> 4) + 2, ((NP * 128) >> 4) + 4,
@@ -398,7 +436,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       const uint32_t idesc_pv =
           umma_idesc_bf16(128, min(NP, mma_width(info[2 * (pv % kInfoRing) + 1].x * G)), true, true);
       tc_fence_after();
-      if (elect_one()) {
+      if (umma_lane<NP>(lane)) {
         // A = V^T: 16 tokens per step (two 8-row groups, SBO 1024; two 64-dim slabs, LBO 16 KB) -> +2048 B;
         // B = P^T: 16 tokens per step (two 8-token core-matrix groups, LBO 128; 8-row groups, SBO 2048) -> +256 B
         constexpr uint32_t kOffV[8] = {0, 128, 256, 384, 512, 640, 768, 896};
@@ -440,15 +478,21 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     }
   } else if (warp >= 4 && ntiles > 0) {
     // ------------------------------------------------------------ softmax / accumulation
-    // Every wait here is warp-uniform and every named barrier ORs "gave up" across the four warps, so the
-    // warps leave the loop together if a wait expires (no warp can be left behind at a barrier).  The barrier
-    // sequence is the same for every row width, so a warp that gave up still matches the others.
-    const int ct = tid - kConsumerBase;       // TMEM lane: token ct of S^T, dim ct of O^T
+    // Warpgroup wg owns rows [rb, rb + HR) of the segment's NR-wide tile (all rows when there is one group).  The
+    // groups share nothing but the S / P / O buffers' barriers: each has its own named barrier (1 + wg) and its
+    // own rows of the shared row arrays.  Every wait here is warp-uniform and every named barrier ORs "gave up"
+    // across the group's four warps, so they leave the loop together if a wait expires; the barrier sequence is
+    // the same for every row width, so a warp that gave up still matches the others.
+    const int cidx = tid - kConsumerBase;
+    const int ct = cidx & 127;                // TMEM lane: token ct of S^T, dim ct of O^T
+    const int wg = cidx >> 7;
     const int wq = ct >> 5;                   // lane quadrant
+    const uint32_t bar_id = 1 + wg;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     const float inv_g = 1.0f / static_cast<float>(G);
     uint8_t* p_smem = smem + C::kP;
-    float l[NP], o[NP], s[NP];
+    constexpr int NPH = C::kRowsPerGroup;
+    float l[NPH], o[NPH], s[NPH];
     int R = 0, nr = 8, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0;
     bool alive = true;
     for (int jj = 0; jj < ntiles; ++jj) {
@@ -470,16 +514,18 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         seg_s0 = KVH * prefix[inf.x] + seg_g * sh.w;
         seg_s1 = seg_s0 + sh.w;
 #pragma unroll
-        for (int r = 0; r < NP; ++r) {
+        for (int r = 0; r < NPH; ++r) {
           l[r] = 0.f;
           o[r] = 0.f;
         }
       }
+      const int hr = C::kWG == 1 ? nr : (nr < 16 ? 8 : nr / 2);   // group_rows at run time
+      const int rb = wg * hr;
       const int tok0 = inf.z * kTileTokens;
       const int tok = tok0 + ct;
       // rows past the sequence end may hold stale or uninitialised values: zero V there so P = 0 cannot meet
-      // a NaN in the PV product (only the last tile of a sequence)
-      if (alive && L - tok0 < kTileTokens) {
+      // a NaN in the PV product (only the last tile of a sequence; group 0 does it before its P arrival)
+      if (alive && wg == 0 && L - tok0 < kTileTokens) {
         alive = mbar_wait_warp(&bars[B_VFULL + st], (jj / kStages) & 1, abort);
         if (alive && tok >= L) {
           uint8_t* vrow = smem + C::kV + st * kTileBytes + ct * 128;
@@ -498,41 +544,40 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         const int d = tok - (L - n);
         const int rmin = d > 0 ? d * G : 0;
         with_rows<NP>(nr, [&](auto nr_c) {
-          constexpr int NR = decltype(nr_c)::value;
-          if constexpr (NR == 8) {
-            tmem_ld8(t_lane + buf * NP, s);
-          } else {
-#pragma unroll
-            for (int c = 0; c < NR; c += 16) tmem_ld16(t_lane + buf * NP + c, s + c);
-          }
+          constexpr int HR = group_rows<NP, decltype(nr_c)::value>();
+          tmem_ld_cols<HR>(t_lane + buf * NP + rb, s);
           tc_fence_before();
           mbar_arrive(&bars[B_SEMPTY + buf]);
 #pragma unroll
-          for (int r = 0; r < NR; ++r) s[r] = (r >= rmin && r < R) ? s[r] * p.scale_log2 : kNegInf;
-          warp_columns<NR, true>(s, red + (buf * 4 + wq) * NP, lane);
+          for (int i = 0; i < HR; ++i) {
+            const int r = rb + i;
+            s[i] = (r >= rmin && r < R) ? s[i] * p.scale_log2 : kNegInf;
+          }
+          warp_columns<HR, true>(s, red + (buf * 4 + wq) * NP + rb, lane);
         });
       }
-      if (named_bar_any(1, 128, !alive)) break;
+      if (named_bar_any(bar_id, 128, !alive)) break;
       // ---- running max (one owner thread per row) and rescale factor
-      if (ct < nr) {
+      if (ct < hr) {
+        const int row = rb + ct;
         float mn = 0.f, alpha = 1.f;
-        if (ct < R) {
+        if (row < R) {
           const float* rr = red + buf * 4 * NP;
-          const float tm = fmaxf(fmaxf(rr[ct], rr[NP + ct]), fmaxf(rr[2 * NP + ct], rr[3 * NP + ct]));
-          const float mo = first ? kNegInf : m_s[ct];
+          const float tm = fmaxf(fmaxf(rr[row], rr[NP + row]), fmaxf(rr[2 * NP + row], rr[3 * NP + row]));
+          const float mo = first ? kNegInf : m_s[row];
           mn = fmaxf(mo, tm);
           alpha = (mn == kNegInf) ? 1.f : fast_exp2(mo - mn);
         }
-        m_s[ct] = mn;
-        alpha_s[buf * NP + ct] = alpha;
+        m_s[row] = mn;
+        alpha_s[buf * NP + row] = alpha;
       }
-      named_bar_sync(1, 128);
+      named_bar_sync(bar_id, 128);
       with_rows<NP>(nr, [&](auto nr_c) {
-        constexpr int NR = decltype(nr_c)::value;
-        const float* ms = m_s;
-        const float* al = alpha_s + buf * NP;
+        constexpr int HR = group_rows<NP, decltype(nr_c)::value>();
+        const float* ms = m_s + rb;
+        const float* al = alpha_s + buf * NP + rb;
 #pragma unroll
-        for (int r = 0; r < NR; r += 4) {
+        for (int r = 0; r < HR; r += 4) {
           const float4 m4 = *reinterpret_cast<const float4*>(ms + r);
           const float4 a4 = *reinterpret_cast<const float4*>(al + r);
           const float mv[4] = {m4.x, m4.y, m4.z, m4.w}, av[4] = {a4.x, a4.y, a4.z, a4.w};
@@ -548,29 +593,20 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           alive = mbar_wait_warp(&bars[B_OFULL], (jj - 1) & 1, abort);
           if (alive) {
             tc_fence_after();
-            const float* ap = alpha_s + (buf ^ 1) * NP;
-            float ot[16];
-            if constexpr (NR == 8) {
-              tmem_ld8(t_lane + 2 * NP, ot);
+            const float* ap = alpha_s + (buf ^ 1) * NP + rb;
+            float ot[HR];
+            tmem_ld_cols<HR>(t_lane + 2 * NP + rb, ot);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) o[i] = o[i] * ap[i] + ot[i];
-            } else {
-#pragma unroll
-              for (int c = 0; c < NR; c += 16) {
-                tmem_ld16(t_lane + 2 * NP + c, ot);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * ap[c + i] + ot[i];
-              }
-            }
+            for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
             tc_fence_before();
           }
         }
         // ---- P^T (bf16), MN-major without swizzle: 8 consecutive rows of token ct form one 16-byte vector.
         // Rows past NR (up to the UMMA N) are never read back: their O^T columns are ignored.
         if (alive) {
-          uint8_t* pb = p_smem + ct * 16;
+          uint8_t* pb = p_smem + ct * 16 + (rb >> 3) * 2048;
 #pragma unroll
-          for (int m = 0; m < NR / 8; ++m) {
+          for (int m = 0; m < HR / 8; ++m) {
             uint4 v;
             v.x = pack_bf16x2(s[8 * m + 0], s[8 * m + 1]);
             v.y = pack_bf16x2(s[8 * m + 2], s[8 * m + 3]);
@@ -585,39 +621,31 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           alive = mbar_wait_warp(&bars[B_OFULL], jj & 1, abort);
           if (alive) {
             tc_fence_after();
-            const float* ap = alpha_s + buf * NP;
-            float ot[16];
-            if constexpr (NR == 8) {
-              tmem_ld8(t_lane + 2 * NP, ot);
+            const float* ap = alpha_s + buf * NP + rb;
+            float ot[HR];
+            tmem_ld_cols<HR>(t_lane + 2 * NP + rb, ot);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) o[i] = o[i] * ap[i] + ot[i];
-            } else {
-#pragma unroll
-              for (int c = 0; c < NR; c += 16) {
-                tmem_ld16(t_lane + 2 * NP + c, ot);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * ap[c + i] + ot[i];
-              }
-            }
+            for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
             tc_fence_before();
-            warp_columns<NR, false>(l, lred + wq * NP, lane);
+            warp_columns<HR, false>(l, lred + wq * NP + rb, lane);
           }
         }
       });
-      if (named_bar_any(1, 128, !alive)) break;
+      if (named_bar_any(bar_id, 128, !alive)) break;
       if (last) {
         const bool complete = (seg_s0 / per) == ((seg_s1 - 1) / per);
         const int slot = 2 * blockIdx.x + (seg_s0 < t_begin ? 0 : 1);
         with_rows<NP>(nr, [&](auto nr_c) {
-          constexpr int NR = decltype(nr_c)::value;
+          constexpr int HR = group_rows<NP, decltype(nr_c)::value>();
 #pragma unroll
-          for (int r = 0; r < NR; ++r) {
+          for (int i = 0; i < HR; ++i) {
+            const int r = rb + i;
             if (r < R) {
               const float lt = lred[r] + lred[NP + r] + lred[2 * NP + r] + lred[3 * NP + r];
-              const float val = lt > 0.f ? o[r] / lt : 0.f;
+              const float val = lt > 0.f ? o[i] / lt : 0.f;
               if (complete) {
-                const int i = __float2int_rz((static_cast<float>(r) + 0.5f) * inv_g), h = r - i * G;
-                p.out[(int64_t)(q0 + i) * p.out_row_stride + (int64_t)(seg_g * G + h) * kHeadDim + ct] =
+                const int qi = __float2int_rz((static_cast<float>(r) + 0.5f) * inv_g), h = r - qi * G;
+                p.out[(int64_t)(q0 + qi) * p.out_row_stride + (int64_t)(seg_g * G + h) * kHeadDim + ct] =
                     __float2bfloat16_rn(val);
               } else {
                 p.part_o[((int64_t)slot * NP + r) * kHeadDim + ct] = val;
@@ -719,7 +747,7 @@ cudaError_t launch_np(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const De
   static_assert(smem <= 232448, "shared memory budget");
   cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  paged_decode_kernel<NP><<<grid, kThreads, smem, stream>>>(tm_k, tm_v, p);
+  paged_decode_kernel<NP><<<grid, Cfg<NP>::kThreads, smem, stream>>>(tm_k, tm_v, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // programmatic dependent launch: the combine kernel's launch and prologue overlap the main kernel's tail
