@@ -59,7 +59,9 @@ struct Cfg {
   static constexpr int kM = kRed + 2 * 4 * NP * 4;               // [NP] running max
   static constexpr int kAlpha = kM + NP * 4;                     // [2][NP] rescale factors
   static constexpr int kLred = kAlpha + 2 * NP * 4;              // [4][NP] column sums per warp
-  static constexpr int kTmem = kLred + 4 * NP * 4;
+  static constexpr int kRowOut = kLred + 4 * NP * 4;             // [NP] per-row output offset (int64)
+  static constexpr int kRowInv = kRowOut + NP * 8;               // [NP] per-row 1 / sum
+  static constexpr int kTmem = kRowInv + NP * 4;
   static constexpr int kAbort = kTmem + 4;
   static constexpr int kScan = kAbort + 4;                       // [16] per-warp prefix totals
   static constexpr int kPrefix = kScan + 64;                     // [kMaxDecodeSeqs + 1]
@@ -279,6 +281,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   float* m_s = reinterpret_cast<float*>(smem + C::kM);
   float* alpha_s = reinterpret_cast<float*>(smem + C::kAlpha);
   float* lred = reinterpret_cast<float*>(smem + C::kLred);
+  int64_t* row_out = reinterpret_cast<int64_t*>(smem + C::kRowOut);
+  float* row_inv = reinterpret_cast<float*>(smem + C::kRowInv);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + C::kAbort);
   int* warp_tot = reinterpret_cast<int*>(smem + C::kScan);
@@ -489,7 +493,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     const int wq = ct >> 5;                   // lane quadrant
     const uint32_t bar_id = 1 + wg;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-    const float inv_g = 1.0f / static_cast<float>(G);
     uint8_t* p_smem = smem + C::kP;
     constexpr int NPH = C::kRowsPerGroup;
     float l[NPH], o[NPH], s[NPH];
@@ -523,19 +526,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       const int rb = wg * hr;
       const int tok0 = inf.z * kTileTokens;
       const int tok = tok0 + ct;
-      // rows past the sequence end may hold stale or uninitialised values: zero V there so P = 0 cannot meet
-      // a NaN in the PV product (only the last tile of a sequence; group 0 does it before its P arrival)
-      if (alive && wg == 0 && L - tok0 < kTileTokens) {
-        alive = mbar_wait_warp(&bars[B_VFULL + st], (jj / kStages) & 1, abort);
-        if (alive && tok >= L) {
-          uint8_t* vrow = smem + C::kV + st * kTileBytes + ct * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-            *reinterpret_cast<uint4*>(vrow + kSlab + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-          }
-        }
-      }
       // ---- S tile -> masked, scaled scores; per-warp column maxima
       alive = alive && mbar_wait_warp(&bars[B_SFULL + buf], (jj >> 1) & 1, abort);
       if (alive) {
@@ -601,6 +591,19 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
             tc_fence_before();
           }
         }
+        // ---- rows past the sequence end may hold stale or uninitialised values: zero V there so P = 0 cannot
+        // meet a NaN in the PV product (last tile of a sequence; group 0, before its P arrival)
+        if (alive && wg == 0 && L - tok0 < kTileTokens) {
+          alive = mbar_wait_warp(&bars[B_VFULL + st], (jj / kStages) & 1, abort);
+          if (alive && tok >= L) {
+            uint8_t* vrow = smem + C::kV + st * kTileBytes + ct * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+              *reinterpret_cast<uint4*>(vrow + kSlab + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
+          }
+        }
         // ---- P^T (bf16), MN-major without swizzle: 8 consecutive rows of token ct form one 16-byte vector.
         // Rows past NR (up to the UMMA N) are never read back: their O^T columns are ignored.
         if (alive) {
@@ -635,21 +638,33 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       if (last) {
         const bool complete = (seg_s0 / per) == ((seg_s1 - 1) / per);
         const int slot = 2 * blockIdx.x + (seg_s0 < t_begin ? 0 : 1);
+        // row owners: 1 / sum, the log2-sum-exp of a piece, and where the row goes
+        if (ct < hr) {
+          const int r = rb + ct;
+          if (r < R) {
+            const float lt = lred[r] + lred[NP + r] + lred[2 * NP + r] + lred[3 * NP + r];
+            row_inv[r] = lt > 0.f ? 1.f / lt : 0.f;
+            if (complete) {
+              const int qi = r / G, h = r - qi * G;
+              row_out[r] = (int64_t)(q0 + qi) * p.out_row_stride + (int64_t)(seg_g * G + h) * kHeadDim;
+            } else {
+              row_out[r] = ((int64_t)slot * NP + r) * kHeadDim;
+              p.part_lse[slot * NP + r] = lt > 0.f ? m_s[r] + __log2f(lt) : kNegInf;
+            }
+          }
+        }
+        named_bar_sync(bar_id, 128);
         with_rows<NP>(nr, [&](auto nr_c) {
           constexpr int HR = group_rows<NP, decltype(nr_c)::value>();
 #pragma unroll
           for (int i = 0; i < HR; ++i) {
             const int r = rb + i;
             if (r < R) {
-              const float lt = lred[r] + lred[NP + r] + lred[2 * NP + r] + lred[3 * NP + r];
-              const float val = lt > 0.f ? o[i] / lt : 0.f;
+              const float val = o[i] * row_inv[r];
               if (complete) {
-                const int qi = __float2int_rz((static_cast<float>(r) + 0.5f) * inv_g), h = r - qi * G;
-                p.out[(int64_t)(q0 + qi) * p.out_row_stride + (int64_t)(seg_g * G + h) * kHeadDim + ct] =
-                    __float2bfloat16_rn(val);
+                p.out[row_out[r] + ct] = __float2bfloat16_rn(val);
               } else {
-                p.part_o[((int64_t)slot * NP + r) * kHeadDim + ct] = val;
-                if (ct == 0) p.part_lse[slot * NP + r] = lt > 0.f ? m_s[r] + __log2f(lt) : kNegInf;
+                p.part_o[row_out[r] + ct] = val;
               }
             }
           }
