@@ -485,6 +485,49 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def profile_case(args):
+    """One workload launched `--steps` times (after `--warmup` launches) and nothing else: the command the ncu
+    summaries under profiles/ capture.  Prints the mean device time per launch (CUDA events, no L2 flush)."""
+    from nvattn import ops
+    from nvattn.workloads import mixed_config, varlen_batch
+    case = args.profile_case
+    if case in ("decode", "verify8"):
+        k = 0 if case == "decode" else 8
+        b, _, H, KVH = decode_shard(1, 0, args.seed if k == 0 else args.seed + 10 + k, B_per_gpu=64 if k == 0 else 32,
+                                    k=k)
+        q = b.q.view(b.num_seqs, k + 1, H, 128)
+        out = torch.empty_like(q)
+
+        def call():
+            ops.flash_attn_with_kvcache(q, b.k_cache, b.v_cache, cache_seqlens=b.context_lens,
+                                        block_table=b.block_tables, softmax_scale=b.scale, out=out)
+    else:
+        if case == "prefill4":
+            chunks, prefixes = [512, 640, 640], [0, 256, 1024]
+            b = varlen_batch(chunks, [c + p for c, p in zip(chunks, prefixes)], 32, 8, 128, 64, 0.5, args.seed + 40,
+                             device="cuda")
+        else:
+            b = mixed_config(seed=args.seed, device="cuda")
+        out = torch.empty_like(b.q)
+
+        def call():
+            ops.flash_attn_varlen_func(b.q, b.k_cache, b.v_cache, max_seqlen_q=b.max_seqlen_q,
+                                       cu_seqlens_q=b.cu_seqlens_q, max_seqlen_k=b.max_seqlen_k,
+                                       cu_seqlens_k=b.cu_seqlens_k, softmax_scale=b.scale, causal=True,
+                                       block_table=b.block_tables, out=out)
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": case, "launches": args.steps,
+                      "us_per_launch": round(e0.elapsed_time(e1) * 1e3 / args.steps, 2)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -494,8 +537,13 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", choices=["decode", "verify8", "prefill4", "mixed4"],
+                    help="run one workload --steps times on one GPU (for ncu captures) and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.profile_case:
+        profile_case(args)
+        return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))

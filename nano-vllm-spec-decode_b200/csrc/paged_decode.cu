@@ -316,13 +316,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
   }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
-    tmem_relinquish();
-  }
   build_prefix(p, prefix, warp_tot, tid, C::kThreads);   // ends with __syncthreads
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
   // let the combine kernel (launched as a programmatic dependent) get resident and run its prologue now; it waits
   // for this grid to finish before it reads any partial
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -332,6 +326,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   const int t_begin = blockIdx.x * per;
   const int t_end = min(total, t_begin + per);
   const int ntiles = t_end > t_begin ? t_end - t_begin : 0;
+  if (ntiles == 0) return;   // nothing for this CTA (e.g. a varlen batch without short runs): no TMEM, no pipeline
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
 
   if ((warp == 0 || warp == 3) && ntiles > 0) {
     // ------------------------------------------------------------ K (warp 0) and V (warp 3) producers
@@ -686,13 +688,17 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   }
 }
 
-// Merge the pieces of segments cut by CTA boundaries, and zero the rows of sequences with no keys.  One warp per
-// query row of the segment; lanes own 4 dims each and walk the pieces with independent loads.
+// Merge the pieces of segments cut by CTA boundaries, and zero the rows of sequences with no keys.  One CTA per cut
+// segment: all (row, piece) log2-sum-exps are loaded at once, row owners turn them into normalised weights, then
+// each thread accumulates (row, 4 dims) over the pieces with independent loads (two dependent memory rounds in
+// all).  Segments with more than 2048 (row, piece) pairs fall back to one warp per row.
 template <int NP>
 __global__ void __launch_bounds__(256)
 paged_decode_combine(const DecodeParams p, int main_grid) {
+  constexpr int kCombineLse = 2048;
   __shared__ int prefix[kMaxDecodeSeqs + 1];
   __shared__ int warp_tot[8];
+  __shared__ float lse_s[kCombineLse];   // [rows][pieces]: log2-sum-exp, then normalised weights
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   build_prefix(p, prefix, warp_tot, tid, 256);
   // everything below reads the main kernel's partials or writes the output: wait for that grid to complete
@@ -721,6 +727,55 @@ paged_decode_combine(const DecodeParams p, int main_grid) {
     const int pieces = c - c0 + 1;
     const SeqShape ss = seq_shape(p, lc.b);
     const int R = ss.n * G;
+    const int64_t out_base = (int64_t)ss.q0 * p.out_row_stride + (int64_t)lc.g * G * kHeadDim;
+    if (R * pieces <= kCombineLse) {
+      // every (row, piece) log2-sum-exp in one round of independent loads
+      for (int idx = tid; idx < R * pieces; idx += 256) {
+        const int r = idx / pieces, pi = idx - r * pieces;
+        const int slot = pi == 0 ? 2 * c0 + 1 : 2 * (c0 + pi);
+        lse_s[idx] = p.part_lse[slot * NP + r];
+      }
+      __syncthreads();
+      // row owners turn them into normalised weights
+      if (tid < R) {
+        float* w = lse_s + tid * pieces;
+        float mx = kNegInf;
+        for (int pi = 0; pi < pieces; ++pi) mx = fmaxf(mx, w[pi]);
+        float den = 0.f;
+        for (int pi = 0; pi < pieces; ++pi) {
+          const float e = (mx == kNegInf || w[pi] == kNegInf) ? 0.f : fast_exp2(w[pi] - mx);
+          w[pi] = e;
+          den += e;
+        }
+        const float inv = den > 0.f ? 1.f / den : 0.f;
+        for (int pi = 0; pi < pieces; ++pi) w[pi] *= inv;
+      }
+      __syncthreads();
+      // (row, 4 dims) per thread; the pieces' loads are independent of each other
+      for (int idx = tid; idx < R * 32; idx += 256) {
+        const int r = idx >> 5, l4 = idx & 31;
+        const float* w = lse_s + r * pieces;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int pi = 0; pi < pieces; ++pi) {
+          const int slot = pi == 0 ? 2 * c0 + 1 : 2 * (c0 + pi);
+          const float4 v = *reinterpret_cast<const float4*>(p.part_o + ((int64_t)slot * NP + r) * kHeadDim + l4 * 4);
+          const float wp = w[pi];
+          acc.x += wp * v.x;
+          acc.y += wp * v.y;
+          acc.z += wp * v.z;
+          acc.w += wp * v.w;
+        }
+        const int i = r / G, h = r - i * G;
+        uint2 packed;
+        packed.x = pack_bf16x2(acc.x, acc.y);
+        packed.y = pack_bf16x2(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(p.out + out_base + (int64_t)i * p.out_row_stride + h * kHeadDim + l4 * 4) = packed;
+      }
+      __syncthreads();   // lse_s is reused by the next segment
+      continue;
+    }
+    // many pieces: one warp per row, walking the pieces
     for (int r = warp; r < R; r += 8) {
       float mx = kNegInf;
       for (int pi = lane; pi < pieces; pi += 32) {
