@@ -32,15 +32,14 @@ namespace nva {
 
 namespace {
 
-constexpr int kStages = 3;
 constexpr int kSlab = 128 * 128;        // 128 rows x 128 bytes (64 bf16 dims)
 constexpr int kTileBytes = 2 * kSlab;   // one K or V tile: dims 0-63 and 64-127
 constexpr int kConsumerBase = 128;
 constexpr float kNegInf = -__builtin_huge_valf();
 constexpr uint32_t kFull = 0xffffffffu;
 // Tile descriptors travel from the K producer to the MMA and softmax warps through a ring of this depth.  The
-// producer runs at most kStages tiles ahead of the S products and those at most 2 ahead of the softmax warps, so
-// an entry is never rewritten before the softmax warps have read it.
+// producer runs at most Cfg::kStages (<= 3) tiles ahead of the S products and those at most 2 ahead of the softmax
+// warps, so an entry is never rewritten before the softmax warps have read it.
 constexpr int kInfoRing = 8;
 
 template <int NP>
@@ -48,7 +47,10 @@ struct Cfg {
   static constexpr int kWG = NP >= 32 ? 2 : 1;                   // softmax warpgroups (row halves)
   static constexpr int kThreads = kConsumerBase + 128 * kWG;
   static constexpr int kRowsPerGroup = NP / kWG;                 // per-thread row arrays
-  static constexpr int kQBuf = NP <= 32 ? 2 : 1;                 // Q double-buffered when shared memory allows
+  // K / V ring depth: 3 tiles; 2 for the 48-row tile, whose softmax needs longer per tile than HBM does (128 KB in
+  // flight per SM still covers the latency) and whose second Q buffer needs the room
+  static constexpr int kStages = NP == 48 ? 2 : 3;
+  static constexpr int kQBuf = 2;                                // Q double buffer: next segment's rows load early
   static constexpr int kK = 0;                                   // K ring
   static constexpr int kV = kStages * kTileBytes;                // V ring
   static constexpr int kQ = 2 * kStages * kTileBytes;            // Q buffers, NP * 256 bytes each
@@ -295,7 +297,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   const int G = p.group;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&bars[B_KFULL + s], 1);
       mbar_init(&bars[B_KEMPTY + s], 1);
       mbar_init(&bars[B_VFULL + s], 1);
@@ -371,12 +373,12 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       const int cnt = min(32, ntiles - base);
       for (int i = 0; i < cnt; ++i) {
         const int jj = base + i;
-        const int st = jj % kStages;
+        const int st = jj % C::kStages;
         const int gi = __shfl_sync(kFull, g, i), ri = __shfl_sync(kFull, row0, i);
         const int bi = __shfl_sync(kFull, b, i), ji = __shfl_sync(kFull, j, i), fi = __shfl_sync(kFull, flags, i);
         const int ni = __shfl_sync(kFull, n, i), Li = __shfl_sync(kFull, L, i), qi = __shfl_sync(kFull, q0, i);
         const int nti = __shfl_sync(kFull, nt, i);
-        if (!mbar_wait_warp(&empty[st], ((jj / kStages) & 1) ^ 1, abort)) {
+        if (!mbar_wait_warp(&empty[st], ((jj / C::kStages) & 1) ^ 1, abort)) {
           stop = true;
           break;
         }
@@ -407,9 +409,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     bool ok = true;
     auto issue_qk = [&]() {
       if (!ok || qk >= ntiles) return;
-      const int st = qk % kStages;
+      const int st = qk % C::kStages;
       const int e = qk % kInfoRing;
-      if (!mbar_wait_warp(&bars[B_KFULL + st], (qk / kStages) & 1, abort)) { ok = false; return; }
+      if (!mbar_wait_warp(&bars[B_KFULL + st], (qk / C::kStages) & 1, abort)) { ok = false; return; }
       const int flags = info[2 * e].w;
       // UMMA N for this tile's segment: its rows rounded up to 16/32/48
       const uint32_t idesc_qk = umma_idesc_bf16(128, min(NP, mma_width(info[2 * e + 1].x * G)), false, false);
@@ -436,9 +438,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     issue_qk();
     issue_qk();
     while (ok && pv < ntiles) {
-      const int st = pv % kStages;
+      const int st = pv % C::kStages;
       if (!mbar_wait_warp(&bars[B_PFULL], pv & 1, abort)) break;
-      if (!mbar_wait_warp(&bars[B_VFULL + st], (pv / kStages) & 1, abort)) break;
+      if (!mbar_wait_warp(&bars[B_VFULL + st], (pv / C::kStages) & 1, abort)) break;
       const uint32_t idesc_pv =
           umma_idesc_bf16(128, min(NP, mma_width(info[2 * (pv % kInfoRing) + 1].x * G)), true, true);
       tc_fence_after();
@@ -501,7 +503,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     int R = 0, nr = 8, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0;
     bool alive = true;
     for (int jj = 0; jj < ntiles; ++jj) {
-      const int st = jj % kStages;
+      const int st = jj % C::kStages;
       const int buf = jj & 1;
       const int e = jj % kInfoRing;
       alive = alive && mbar_wait_warp(&bars[B_INFO + e], (jj / kInfoRing) & 1, abort);
@@ -528,6 +530,18 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       const int rb = wg * hr;
       const int tok0 = inf.z * kTileTokens;
       const int tok = tok0 + ct;
+      if (C::kWG == 2 && rb >= R) {
+        // every row of this group is padding (a short segment): only keep the S / P / O phases paced.  SEMPTY of
+        // tile jj is given after S(jj) exists, PFULL of jj after PV(jj-1) finished, as the working group does, so
+        // no arrival can land in a phase that the other group has not reached.
+        alive = alive && mbar_wait_warp(&bars[B_SFULL + buf], (jj >> 1) & 1, abort);
+        if (alive) mbar_arrive(&bars[B_SEMPTY + buf]);
+        if (!first) alive = alive && mbar_wait_warp(&bars[B_OFULL], (jj - 1) & 1, abort);
+        if (alive) mbar_arrive(&bars[B_PFULL]);
+        if (last) alive = alive && mbar_wait_warp(&bars[B_OFULL], jj & 1, abort);
+        if (named_bar_any(bar_id, 128, !alive)) break;
+        continue;
+      }
       // ---- S tile -> masked, scaled scores; per-warp column maxima
       alive = alive && mbar_wait_warp(&bars[B_SFULL + buf], (jj >> 1) & 1, abort);
       if (alive) {
@@ -596,7 +610,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         // ---- rows past the sequence end may hold stale or uninitialised values: zero V there so P = 0 cannot
         // meet a NaN in the PV product (last tile of a sequence; group 0, before its P arrival)
         if (alive && wg == 0 && L - tok0 < kTileTokens) {
-          alive = mbar_wait_warp(&bars[B_VFULL + st], (jj / kStages) & 1, abort);
+          alive = mbar_wait_warp(&bars[B_VFULL + st], (jj / C::kStages) & 1, abort);
           if (alive && tok >= L) {
             uint8_t* vrow = smem + C::kV + st * kTileBytes + ct * 128;
 #pragma unroll
