@@ -47,9 +47,9 @@ struct Cfg {
   static constexpr int kWG = NP >= 32 ? 2 : 1;                   // softmax warpgroups (row halves)
   static constexpr int kThreads = kConsumerBase + 128 * kWG;
   static constexpr int kRowsPerGroup = NP / kWG;                 // per-thread row arrays
-  // K / V ring depth: 3 tiles; 2 for the 48-row tile, whose softmax needs longer per tile than HBM does (128 KB in
-  // flight per SM still covers the latency) and whose second Q buffer needs the room
-  static constexpr int kStages = NP == 48 ? 2 : 3;
+  // K / V ring depth: 3 tiles; 2 for the 32/48-row tiles, whose softmax needs longer per tile than HBM does (128 KB
+  // in flight per SM still covers the latency) and whose second Q buffer needs the room
+  static constexpr int kStages = NP >= 32 ? 2 : 3;
   static constexpr int kQBuf = 2;                                // Q double buffer: next segment's rows load early
   static constexpr int kK = 0;                                   // K ring
   static constexpr int kV = kStages * kTileBytes;                // V ring
@@ -65,9 +65,10 @@ struct Cfg {
   static constexpr int kRowInv = kRowOut + NP * 8;               // [NP] per-row 1 / sum
   static constexpr int kTmem = kRowInv + NP * 4;
   static constexpr int kAbort = kTmem + 4;
-  static constexpr int kScan = kAbort + 4;                       // [16] per-warp prefix totals
-  static constexpr int kPrefix = kScan + 64;                     // [kMaxDecodeSeqs + 1]
-  static constexpr int kEnd = kPrefix + (kMaxDecodeSeqs + 1) * 4;
+  static constexpr int kScan = (kAbort + 4 + 7) & ~7;            // [16] int2 per-warp prefix totals
+  static constexpr int kPrefix = kScan + 16 * 8;                 // [kMaxDecodeSeqs + 1] tiles
+  static constexpr int kCPrefix = kPrefix + (kMaxDecodeSeqs + 1) * 4;   // [kMaxDecodeSeqs + 1] cost units
+  static constexpr int kEnd = kCPrefix + (kMaxDecodeSeqs + 1) * 4;
   static constexpr int kBytes = kEnd + 1024;                     // + slack for 1024-byte alignment
 };
 
@@ -103,37 +104,94 @@ __device__ __forceinline__ int seq_tiles(const DecodeParams& p, int b) {
   return (s.L + kTileTokens - 1) / kTileTokens;
 }
 
-// Exclusive prefix sum of per-sequence tile counts into prefix[0..B] (prefix[B] = total per kv head).
-// Called by all `nthreads` threads of the block; ends with a __syncthreads.
-__device__ void build_prefix(const DecodeParams& p, int* prefix, int* warp_tot, int tid, int nthreads) {
+// Cost of a (sequence, kv head) segment in the work split, in tile units: its tiles plus this much for the segment's
+// start and end (Q load, first-tile latency, final PV, normalisation, output), measured on B200 at about two tiles.
+constexpr int kSegCost = 2;
+
+// Exclusive prefix sums over the sequences, per kv head: prefix[b] = tiles before sequence b, cprefix[b] = cost units
+// before it (tiles + kSegCost per non-empty segment; padding sequences add nothing).  Called by all `nthreads`
+// threads of the block; ends with a __syncthreads.
+__device__ void build_prefix(const DecodeParams& p, int* prefix, int* cprefix, int2* warp_tot, int tid,
+                             int nthreads) {
   const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
-  int running = 0;
+  int running = 0, crunning = 0;
   for (int base = 0; base < p.num_seqs; base += nthreads) {
     const int b = base + tid;
     const int v = b < p.num_seqs ? seq_tiles(p, b) : 0;
-    int x = v;
+    const int cv = v > 0 ? v + kSegCost : 0;
+    int x = v, cx = cv;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(kFull, x, o);
-      if (lane >= o) x += y;
+      const int y = __shfl_up_sync(kFull, x, o), cy = __shfl_up_sync(kFull, cx, o);
+      if (lane >= o) {
+        x += y;
+        cx += cy;
+      }
     }
-    if (lane == 31) warp_tot[warp] = x;
+    if (lane == 31) warp_tot[warp] = make_int2(x, cx);
     __syncthreads();
-    int before = running, chunk = 0;
+    int before = running, cbefore = crunning, chunk = 0, cchunk = 0;
     for (int w = 0; w < nwarps; ++w) {
-      if (w < warp) before += warp_tot[w];
-      chunk += warp_tot[w];
+      const int2 wt = warp_tot[w];
+      if (w < warp) {
+        before += wt.x;
+        cbefore += wt.y;
+      }
+      chunk += wt.x;
+      cchunk += wt.y;
     }
-    if (b < p.num_seqs) prefix[b] = before + x - v;
+    if (b < p.num_seqs) {
+      prefix[b] = before + x - v;
+      cprefix[b] = cbefore + cx - cv;
+    }
     running += chunk;
+    crunning += cchunk;
     __syncthreads();
   }
-  if (tid == 0) prefix[p.num_seqs] = running;
+  if (tid == 0) {
+    prefix[p.num_seqs] = running;
+    cprefix[p.num_seqs] = crunning;
+  }
   __syncthreads();
 }
 
 struct Loc {
   int b, g, j, nt, s0;
+};
+
+// Cost-weighted split of the tiles over `grid` CTAs.  Tile j of segment (b, g) sits at cost position
+// KVH * cprefix[b] + g * (nt + kSegCost) + kSegCost + j; CTA c owns the tiles whose positions fall in
+// [c * per, (c + 1) * per), a contiguous range of global tile indices.  It depends only on the lengths.
+struct Split {
+  const int* prefix;
+  const int* cprefix;
+  int B, KVH, per, tiles;
+  __device__ Split(const int* pf, const int* cpf, int nseq, int kvh, int grid) : prefix(pf), cprefix(cpf), B(nseq),
+                                                                                KVH(kvh) {
+    tiles = KVH * prefix[B];
+    const int cost = KVH * cprefix[B];
+    per = cost > 0 ? (cost + grid - 1) / grid : 1;
+  }
+  __device__ int pos(int b, int g, int j) const {
+    const int nt = prefix[b + 1] - prefix[b];
+    return KVH * cprefix[b] + g * (nt + kSegCost) + kSegCost + j;
+  }
+  __device__ int owner(int b, int g, int j) const { return pos(b, g, j) / per; }
+  // first global tile index of CTA c (tiles when c owns nothing further)
+  __device__ int begin(int c) const {
+    const int x = c * per;
+    if (x >= KVH * cprefix[B]) return tiles;
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (KVH * cprefix[mid] <= x) lo = mid; else hi = mid - 1;
+    }
+    const int nt = prefix[lo + 1] - prefix[lo];
+    const int rem = x - KVH * cprefix[lo];
+    const int g = rem / (nt + kSegCost);
+    const int o = rem - g * (nt + kSegCost);
+    return KVH * prefix[lo] + g * nt + max(0, o - kSegCost);
+  }
 };
 
 // Global tile t -> (sequence, kv head, tile within segment).  Requires t < KVH * prefix[B].
@@ -287,8 +345,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   float* row_inv = reinterpret_cast<float*>(smem + C::kRowInv);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + C::kAbort);
-  int* warp_tot = reinterpret_cast<int*>(smem + C::kScan);
+  int2* warp_tot = reinterpret_cast<int2*>(smem + C::kScan);
   int* prefix = reinterpret_cast<int*>(smem + C::kPrefix);
+  int* cprefix = reinterpret_cast<int*>(smem + C::kCPrefix);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -318,15 +377,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
   }
-  build_prefix(p, prefix, warp_tot, tid, C::kThreads);   // ends with __syncthreads
+  build_prefix(p, prefix, cprefix, warp_tot, tid, C::kThreads);   // ends with __syncthreads
   // let the combine kernel (launched as a programmatic dependent) get resident and run its prologue now; it waits
   // for this grid to finish before it reads any partial
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  const int total = KVH * prefix[p.num_seqs];
-  const int per = total > 0 ? (total + gridDim.x - 1) / gridDim.x : 1;
-  const int t_begin = blockIdx.x * per;
-  const int t_end = min(total, t_begin + per);
+  const Split split(prefix, cprefix, p.num_seqs, KVH, gridDim.x);
+  const int t_begin = split.begin(blockIdx.x);
+  const int t_end = split.begin(blockIdx.x + 1);
   const int ntiles = t_end > t_begin ? t_end - t_begin : 0;
   if (ntiles == 0) return;   // nothing for this CTA (e.g. a varlen batch without short runs): no TMEM, no pipeline
   if (warp == 1) {
@@ -500,7 +558,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     uint8_t* p_smem = smem + C::kP;
     constexpr int NPH = C::kRowsPerGroup;
     float l[NPH], o[NPH], s[NPH];
-    int R = 0, nr = 8, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0;
+    int R = 0, nr = 8, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0, seg_b = 0;
     bool alive = true;
     for (int jj = 0; jj < ntiles; ++jj) {
       const int st = jj % C::kStages;
@@ -516,6 +574,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         L = sh.y;
         q0 = sh.z;
         seg_g = inf.y;
+        seg_b = inf.x;
         R = n * G;
         nr = min(NP, rows_width(R));
         seg_s0 = KVH * prefix[inf.x] + seg_g * sh.w;
@@ -652,7 +711,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       });
       if (named_bar_any(bar_id, 128, !alive)) break;
       if (last) {
-        const bool complete = (seg_s0 / per) == ((seg_s1 - 1) / per);
+        const bool complete = split.owner(seg_b, seg_g, 0) == split.owner(seg_b, seg_g, seg_s1 - seg_s0 - 1);
         const int slot = 2 * blockIdx.x + (seg_s0 < t_begin ? 0 : 1);
         // row owners: 1 / sum, the log2-sum-exp of a piece, and where the row goes
         if (ct < hr) {
@@ -711,10 +770,11 @@ __global__ void __launch_bounds__(256)
 paged_decode_combine(const DecodeParams p, int main_grid) {
   constexpr int kCombineLse = 2048;
   __shared__ int prefix[kMaxDecodeSeqs + 1];
-  __shared__ int warp_tot[8];
+  __shared__ int cprefix[kMaxDecodeSeqs + 1];
+  __shared__ int2 warp_tot[8];
   __shared__ float lse_s[kCombineLse];   // [rows][pieces]: log2-sum-exp, then normalised weights
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  build_prefix(p, prefix, warp_tot, tid, 256);
+  build_prefix(p, prefix, cprefix, warp_tot, tid, 256);
   // everything below reads the main kernel's partials or writes the output: wait for that grid to complete
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int KVH = p.num_kv_heads, G = p.group;
@@ -729,15 +789,14 @@ paged_decode_combine(const DecodeParams p, int main_grid) {
       }
     }
   }
-  const int total = KVH * prefix[p.num_seqs];
-  const int per = total > 0 ? (total + main_grid - 1) / main_grid : 1;
+  const Split split(prefix, cprefix, p.num_seqs, KVH, main_grid);
   for (int c = blockIdx.x; c < main_grid; c += gridDim.x) {
-    const int t = c * per;
-    if (c == 0 || t >= total) continue;
+    const int t = split.begin(c);
+    if (c == 0 || t >= split.tiles) continue;
     const Loc lc = locate(t, prefix, p.num_seqs, KVH);
-    const int s1 = lc.s0 + lc.nt;
-    if (lc.s0 >= t || (s1 - 1) / per != c) continue;   // not a cut segment ending in CTA c
-    const int c0 = lc.s0 / per;
+    // a cut segment ending in CTA c: it started before c's first tile and its last tile is c's
+    if (lc.s0 >= t || split.owner(lc.b, lc.g, lc.nt - 1) != c) continue;
+    const int c0 = split.owner(lc.b, lc.g, 0);
     const int pieces = c - c0 + 1;
     const SeqShape ss = seq_shape(p, lc.b);
     const int R = ss.n * G;
