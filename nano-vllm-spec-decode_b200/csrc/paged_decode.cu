@@ -38,7 +38,7 @@ constexpr int kConsumerBase = 128;
 constexpr float kNegInf = -__builtin_huge_valf();
 constexpr uint32_t kFull = 0xffffffffu;
 // Tile descriptors travel from the K producer to the MMA and softmax warps through a ring of this depth.  The
-// producer runs at most Cfg::kStages (<= 3) tiles ahead of the S products and those at most 2 ahead of the softmax
+// producer runs at most Cfg::kKStages (<= 3) tiles ahead of the S products and those at most 2 ahead of the softmax
 // warps, so an entry is never rewritten before the softmax warps have read it.
 constexpr int kInfoRing = 8;
 
@@ -47,13 +47,14 @@ struct Cfg {
   static constexpr int kWG = NP >= 32 ? 2 : 1;                   // softmax warpgroups (row halves)
   static constexpr int kThreads = kConsumerBase + 128 * kWG;
   static constexpr int kRowsPerGroup = NP / kWG;                 // per-thread row arrays
-  // K / V ring depth: 3 tiles; 2 for the 32/48-row tiles, whose softmax needs longer per tile than HBM does (128 KB
-  // in flight per SM still covers the latency) and whose second Q buffer needs the room
-  static constexpr int kStages = NP >= 32 ? 2 : 3;
+  // Ring depths: 3 tiles; 2 for the 32/48-row tiles, whose softmax needs longer per tile than HBM does and whose
+  // second Q buffer needs the room (a third V stage there measured slightly slower: 228 vs 221 us on config 4)
+  static constexpr int kKStages = NP >= 32 ? 2 : 3;
+  static constexpr int kVStages = NP >= 32 ? 2 : 3;
   static constexpr int kQBuf = 2;                                // Q double buffer: next segment's rows load early
   static constexpr int kK = 0;                                   // K ring
-  static constexpr int kV = kStages * kTileBytes;                // V ring
-  static constexpr int kQ = 2 * kStages * kTileBytes;            // Q buffers, NP * 256 bytes each
+  static constexpr int kV = kKStages * kTileBytes;               // V ring
+  static constexpr int kQ = (kKStages + kVStages) * kTileBytes;  // Q buffers, NP * 256 bytes each
   static constexpr int kP = kQ + kQBuf * NP * 256;               // P^T, NP * 256 bytes
   static constexpr int kBars = kP + NP * 256;                    // 32 x u64
   static constexpr int kInfo = kBars + 32 * 8;                   // kInfoRing x 2 x int4
@@ -356,9 +357,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   const int G = p.group;
 
   if (tid == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
+    for (int s = 0; s < C::kKStages; ++s) {
       mbar_init(&bars[B_KFULL + s], 1);
       mbar_init(&bars[B_KEMPTY + s], 1);
+    }
+    for (int s = 0; s < C::kVStages; ++s) {
       mbar_init(&bars[B_VFULL + s], 1);
       mbar_init(&bars[B_VEMPTY + s], 1);
     }
@@ -402,6 +405,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     uint8_t* ring = smem + (is_k ? C::kK : C::kV);
     uint64_t* full = bars + (is_k ? B_KFULL : B_VFULL);
     uint64_t* empty = bars + (is_k ? B_KEMPTY : B_VEMPTY);
+    const int stages = is_k ? C::kKStages : C::kVStages;
     bool stop = false;
     for (int base = 0; base < ntiles && !stop; base += 32) {
       // lane-parallel descriptors of the next 32 tiles (the block-table reads overlap each other)
@@ -431,12 +435,12 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       const int cnt = min(32, ntiles - base);
       for (int i = 0; i < cnt; ++i) {
         const int jj = base + i;
-        const int st = jj % C::kStages;
+        const int st = jj % stages;
         const int gi = __shfl_sync(kFull, g, i), ri = __shfl_sync(kFull, row0, i);
         const int bi = __shfl_sync(kFull, b, i), ji = __shfl_sync(kFull, j, i), fi = __shfl_sync(kFull, flags, i);
         const int ni = __shfl_sync(kFull, n, i), Li = __shfl_sync(kFull, L, i), qi = __shfl_sync(kFull, q0, i);
         const int nti = __shfl_sync(kFull, nt, i);
-        if (!mbar_wait_warp(&empty[st], ((jj / C::kStages) & 1) ^ 1, abort)) {
+        if (!mbar_wait_warp(&empty[st], ((jj / stages) & 1) ^ 1, abort)) {
           stop = true;
           break;
         }
@@ -467,9 +471,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     bool ok = true;
     auto issue_qk = [&]() {
       if (!ok || qk >= ntiles) return;
-      const int st = qk % C::kStages;
+      const int st = qk % C::kKStages;
       const int e = qk % kInfoRing;
-      if (!mbar_wait_warp(&bars[B_KFULL + st], (qk / C::kStages) & 1, abort)) { ok = false; return; }
+      if (!mbar_wait_warp(&bars[B_KFULL + st], (qk / C::kKStages) & 1, abort)) { ok = false; return; }
       const int flags = info[2 * e].w;
       // UMMA N for this tile's segment: its rows rounded up to 16/32/48
       const uint32_t idesc_qk = umma_idesc_bf16(128, min(NP, mma_width(info[2 * e + 1].x * G)), false, false);
@@ -496,9 +500,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     issue_qk();
     issue_qk();
     while (ok && pv < ntiles) {
-      const int st = pv % C::kStages;
+      const int st = pv % C::kVStages;
       if (!mbar_wait_warp(&bars[B_PFULL], pv & 1, abort)) break;
-      if (!mbar_wait_warp(&bars[B_VFULL + st], (pv / C::kStages) & 1, abort)) break;
+      if (!mbar_wait_warp(&bars[B_VFULL + st], (pv / C::kVStages) & 1, abort)) break;
       const uint32_t idesc_pv =
           umma_idesc_bf16(128, min(NP, mma_width(info[2 * (pv % kInfoRing) + 1].x * G)), true, true);
       tc_fence_after();
@@ -561,7 +565,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     int R = 0, nr = 8, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0, seg_b = 0;
     bool alive = true;
     for (int jj = 0; jj < ntiles; ++jj) {
-      const int st = jj % C::kStages;
+      const int st = jj % C::kVStages;      // V ring slot of this tile
       const int buf = jj & 1;
       const int e = jj % kInfoRing;
       alive = alive && mbar_wait_warp(&bars[B_INFO + e], (jj / kInfoRing) & 1, abort);
@@ -669,7 +673,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         // ---- rows past the sequence end may hold stale or uninitialised values: zero V there so P = 0 cannot
         // meet a NaN in the PV product (last tile of a sequence; group 0, before its P arrival)
         if (alive && wg == 0 && L - tok0 < kTileTokens) {
-          alive = mbar_wait_warp(&bars[B_VFULL + st], (jj / C::kStages) & 1, abort);
+          alive = mbar_wait_warp(&bars[B_VFULL + st], (jj / C::kVStages) & 1, abort);
           if (alive && tok >= L) {
             uint8_t* vrow = smem + C::kV + st * kTileBytes + ct * 128;
 #pragma unroll
