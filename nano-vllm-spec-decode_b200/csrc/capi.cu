@@ -179,8 +179,7 @@ NVA_API int nva_paged_decode(const void* q, int64_t q_row_stride, const void* k_
   p.block_size = block_size;
   p.num_blocks = num_blocks;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
-  p.part_o = static_cast<float*>(workspace);
-  p.part_lse = p.part_o + static_cast<size_t>(2) * grid * np * nva::kHeadDim;
+  nva::decode_workspace_layout(workspace, grid, np, &p);
   cudaError_t e = nva::launch_paged_decode(tm_k, tm_v, p, np, grid, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? NVA_OK : cuda_fail(e);
 }
@@ -272,8 +271,7 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
     p.block_size = block_size;
     p.num_blocks = num_blocks;
     p.scale_log2 = softmax_scale * 1.4426950408889634f;
-    p.part_o = static_cast<float*>(workspace);
-    p.part_lse = p.part_o + static_cast<size_t>(2) * grid * np * nva::kHeadDim;
+    nva::decode_workspace_layout(workspace, grid, np, &p);
     cudaError_t e = nva::launch_paged_decode(tm_k, tm_v, p, np, grid, s);
     if (e != cudaSuccess) return cuda_fail(e);
   }

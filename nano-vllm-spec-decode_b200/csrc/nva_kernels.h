@@ -37,9 +37,13 @@ struct DecodeParams {
   float scale_log2;
   float* part_o;     // [2 * grid, NP, 128] split partial outputs (normalised)
   float* part_lse;   // [2 * grid, NP] their log2-sum-exp
+  int32_t* counters; // [grid][2] merge tickets per cut segment (CTA of its first piece) and softmax group: zero on
+                     // entry and on exit
 };
 
 size_t decode_workspace_bytes(int grid, int np);
+// Carve the workspace (decode_workspace_bytes(grid, np) bytes) into the partials and the merge counters.
+void decode_workspace_layout(void* ws, int grid, int np, DecodeParams* p);
 int decode_rows_padded(int rows);  // 16, 32 or 48 (0 if too many)
 cudaError_t launch_paged_decode(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const DecodeParams& p, int np,
                                 int grid, cudaStream_t stream);

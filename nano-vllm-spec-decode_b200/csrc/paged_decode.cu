@@ -9,9 +9,10 @@
 //                                              B = P^T    (MN-major, no swizzle, 16-byte stores per thread)
 // so one HBM pass over each KV block serves every q head of its group and every draft position.
 //
-// Work split: every CTA is persistent (one per SM) and owns an equal share of the 128-token tiles of all
+// Work split: every CTA is persistent (one per SM) and owns a cost-weighted share of the 128-token tiles of all
 // (sequence, kv head) segments, in (sequence, kv head, tile) order.  A segment inside one CTA is finished there;
-// one cut by a CTA boundary leaves a normalised partial + log2-sum-exp per piece, merged by paged_decode_combine.
+// one cut by a CTA boundary leaves a normalised partial + log2-sum-exp per piece, and the last piece to finish
+// (counted with an atomic ticket) merges them all in the same launch.
 // The split depends only on the batch's lengths (padding sequences of length 0 change nothing), and there is no
 // host value or device read-back involved: graph-capturable with a fixed launch geometry.
 //
@@ -42,6 +43,8 @@ constexpr uint32_t kFull = 0xffffffffu;
 // warps, so an entry is never rewritten before the softmax warps have read it.
 constexpr int kInfoRing = 8;
 
+constexpr int kMergePieces = 16;   // pieces of a cut segment merged through the shared weight table
+
 template <int NP>
 struct Cfg {
   static constexpr int kWG = NP >= 32 ? 2 : 1;                   // softmax warpgroups (row halves)
@@ -64,7 +67,8 @@ struct Cfg {
   static constexpr int kLred = kAlpha + 2 * NP * 4;              // [4][NP] column sums per warp
   static constexpr int kRowOut = kLred + 4 * NP * 4;             // [NP] per-row output offset (int64)
   static constexpr int kRowInv = kRowOut + NP * 8;               // [NP] per-row 1 / sum
-  static constexpr int kTmem = kRowInv + NP * 4;
+  static constexpr int kMergeW = kRowInv + NP * 4;               // [kWG][NP][kMergePieces] merge weights
+  static constexpr int kTmem = kMergeW + kWG * NP * kMergePieces * 4;
   static constexpr int kAbort = kTmem + 4;
   static constexpr int kScan = (kAbort + 4 + 7) & ~7;            // [16] int2 per-warp prefix totals
   static constexpr int kPrefix = kScan + 16 * 8;                 // [kMaxDecodeSeqs + 1] tiles
@@ -329,6 +333,131 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
   }
 }
 
+// Merge the pieces of a cut segment (CTAs c0..c1) into its output rows [r0, r1), from one 128-thread group (all of
+// its threads call this; named barrier bar_id).  Each piece is weighted by 2^(lse - max lse) / sum.  The partials were
+// written by other CTAs, so they are read past L1 (ld.global.cg).  Two pieces: (row, 4 dims) items six at a time
+// with all their loads in one round.  Up to kMergePieces pieces: one thread per row puts the row's weights in the
+// group's table `wsm`, then items four at a time (two memory rounds).  More pieces: a plain loop.
+template <int NP>
+__device__ __forceinline__ void merge_pieces(const DecodeParams& p, int c0, int c1, int r0, int r1, int G,
+                                             int64_t out_base, int ct, float* wsm, uint32_t bar_id) {
+  const int pieces = c1 - c0 + 1;
+  auto slot_of = [&](int pi) { return pi == 0 ? 2 * c0 + 1 : 2 * (c0 + pi); };
+  auto store = [&](int idx, float4 a, float inv) {
+    const int r = r0 + (idx >> 5), l4 = idx & 31;
+    const int i = r / G, h = r - i * G;
+    uint2 packed;
+    packed.x = pack_bf16x2(a.x * inv, a.y * inv);
+    packed.y = pack_bf16x2(a.z * inv, a.w * inv);
+    *reinterpret_cast<uint2*>(p.out + out_base + (int64_t)i * p.out_row_stride + h * kHeadDim + l4 * 4) = packed;
+  };
+  if (pieces == 2) {
+    // a segment cut once (the usual case): every load of a round of six items issued together
+    const int s0 = 2 * c0 + 1, s1 = 2 * c0 + 2;
+    const int nitems = (r1 - r0) * 32;
+    constexpr int kRound = 2;
+    for (int base = ct; base < nitems; base += kRound * 128) {
+      float4 a0[kRound], a1[kRound];
+      float e0[kRound], e1[kRound];
+#pragma unroll
+      for (int u = 0; u < kRound; ++u) {
+        const int idx = base + u * 128;
+        if (idx < nitems) {
+          const int r = r0 + (idx >> 5), l4 = idx & 31;
+          e0[u] = __ldcg(p.part_lse + s0 * NP + r);
+          e1[u] = __ldcg(p.part_lse + s1 * NP + r);
+          a0[u] = __ldcg(reinterpret_cast<const float4*>(p.part_o + ((int64_t)s0 * NP + r) * kHeadDim) + l4);
+          a1[u] = __ldcg(reinterpret_cast<const float4*>(p.part_o + ((int64_t)s1 * NP + r) * kHeadDim) + l4);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kRound; ++u) {
+        const int idx = base + u * 128;
+        if (idx < nitems) {
+          const float mx = fmaxf(e0[u], e1[u]);
+          const float w0 = (mx == kNegInf || e0[u] == kNegInf) ? 0.f : fast_exp2(e0[u] - mx);
+          const float w1 = (mx == kNegInf || e1[u] == kNegInf) ? 0.f : fast_exp2(e1[u] - mx);
+          const float den = w0 + w1;
+          const float4 acc = make_float4(w0 * a0[u].x + w1 * a1[u].x, w0 * a0[u].y + w1 * a1[u].y,
+                                         w0 * a0[u].z + w1 * a1[u].z, w0 * a0[u].w + w1 * a1[u].w);
+          store(idx, acc, den > 0.f ? 1.f / den : 0.f);
+        }
+      }
+    }
+    return;
+  }
+  if (pieces <= kMergePieces) {
+    for (int r = r0 + ct; r < r1; r += 128) {
+      float* w = wsm + (r - r0) * kMergePieces;
+      float mx = kNegInf;
+      for (int pi = 0; pi < pieces; ++pi) {
+        const float v = __ldcg(p.part_lse + slot_of(pi) * NP + r);
+        w[pi] = v;
+        mx = fmaxf(mx, v);
+      }
+      float den = 0.f;
+      for (int pi = 0; pi < pieces; ++pi) {
+        const float e = (mx == kNegInf || w[pi] == kNegInf) ? 0.f : fast_exp2(w[pi] - mx);
+        w[pi] = e;
+        den += e;
+      }
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      for (int pi = 0; pi < pieces; ++pi) w[pi] *= inv;
+    }
+    named_bar_sync(bar_id, 128);
+    const int nitems = (r1 - r0) * 32;
+    for (int base = ct; base < nitems; base += 4 * 128) {
+      float4 acc[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int idx = base + u * 128;
+        if (idx < nitems) {
+          const int r = r0 + (idx >> 5), l4 = idx & 31;
+          const float* w = wsm + (r - r0) * kMergePieces;
+          for (int pi = 0; pi < pieces; ++pi) {
+            const float4 v =
+                __ldcg(reinterpret_cast<const float4*>(p.part_o + ((int64_t)slot_of(pi) * NP + r) * kHeadDim) + l4);
+            const float wp = w[pi];
+            acc[u].x += wp * v.x;
+            acc[u].y += wp * v.y;
+            acc[u].z += wp * v.z;
+            acc[u].w += wp * v.w;
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = base + u * 128;
+        if (idx < nitems) store(idx, acc[u], 1.f);
+      }
+    }
+    return;
+  }
+  for (int idx = ct; idx < (r1 - r0) * 32; idx += 128) {
+    const int r = r0 + (idx >> 5), l4 = idx & 31;
+    float mx = kNegInf;
+    for (int pi = 0; pi < pieces; ++pi) mx = fmaxf(mx, __ldcg(p.part_lse + slot_of(pi) * NP + r));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float den = 0.f;
+    if (mx != kNegInf) {
+#pragma unroll 4
+      for (int pi = 0; pi < pieces; ++pi) {
+        const float lse = __ldcg(p.part_lse + slot_of(pi) * NP + r);
+        const float4 v =
+            __ldcg(reinterpret_cast<const float4*>(p.part_o + ((int64_t)slot_of(pi) * NP + r) * kHeadDim) + l4);
+        const float w = lse == kNegInf ? 0.f : fast_exp2(lse - mx);
+        acc.x += w * v.x;
+        acc.y += w * v.y;
+        acc.z += w * v.z;
+        acc.w += w * v.w;
+        den += w;
+      }
+    }
+    store(idx, acc, den > 0.f ? 1.f / den : 0.f);
+  }
+}
+
 template <int NP>
 __global__ void __launch_bounds__(Cfg<NP>::kThreads, 1)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -344,6 +473,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   float* lred = reinterpret_cast<float*>(smem + C::kLred);
   int64_t* row_out = reinterpret_cast<int64_t*>(smem + C::kRowOut);
   float* row_inv = reinterpret_cast<float*>(smem + C::kRowInv);
+  float* merge_w = reinterpret_cast<float*>(smem + C::kMergeW);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + C::kAbort);
   int2* warp_tot = reinterpret_cast<int2*>(smem + C::kScan);
@@ -381,9 +511,17 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     tma_prefetch_desc(&tm_v);
   }
   build_prefix(p, prefix, cprefix, warp_tot, tid, C::kThreads);   // ends with __syncthreads
-  // let the combine kernel (launched as a programmatic dependent) get resident and run its prologue now; it waits
-  // for this grid to finish before it reads any partial
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // sequences whose query rows see no key (length 0: batch padding) get zero rows, from CTA b % grid
+  for (int b = blockIdx.x; b < p.num_seqs; b += gridDim.x) {
+    const SeqShape ss = seq_shape(p, b);
+    if (ss.n >= 1 && ss.n <= p.max_n && ss.L < 1) {
+      const int per_row = p.num_heads * kHeadDim;
+      for (int idx = tid; idx < ss.n * per_row; idx += C::kThreads) {
+        const int i = idx / per_row, rem = idx - i * per_row;
+        p.out[(int64_t)(ss.q0 + i) * p.out_row_stride + rem] = __float2bfloat16_rn(0.f);
+      }
+    }
+  }
 
   const Split split(prefix, cprefix, p.num_seqs, KVH, gridDim.x);
   const int t_begin = split.begin(blockIdx.x);
@@ -564,6 +702,27 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     float l[NPH], o[NPH], s[NPH];
     int R = 0, nr = 8, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0, seg_b = 0;
     bool alive = true;
+    // A piece of a cut segment is done (this group's rows [rb, rb + hr) written): take the group's ticket for the
+    // segment; the group that brings it to the number of pieces merges those rows of all pieces and puts the
+    // counter back to zero, so the counters are zero again when the launch ends (the workspace contract).  Every
+    // thread of the group calls this.
+    auto arrive_and_merge = [&](int c0, int c1, int rb_, int hr_) {
+      named_bar_sync(bar_id, 128);
+      bool last_arrival = false;
+      if (ct == 0) {
+        int32_t* ticket = p.counters + 2 * c0 + wg;
+        __threadfence();   // release: the group's partial rows (ordered before by the barrier) before the ticket
+        last_arrival = atomicAdd(ticket, 1) == c1 - c0;
+        if (last_arrival) {
+          __threadfence();   // acquire: the other pieces' rows, for the whole group after the barrier below
+          *ticket = 0;
+        }
+      }
+      if (named_bar_any(bar_id, 128, last_arrival))
+        merge_pieces<NP>(p, c0, c1, rb_, min(rb_ + hr_, R), G,
+                         (int64_t)q0 * p.out_row_stride + (int64_t)seg_g * G * kHeadDim, ct,
+                         merge_w + wg * NP * kMergePieces, bar_id);
+    };
     for (int jj = 0; jj < ntiles; ++jj) {
       const int st = jj % C::kVStages;      // V ring slot of this tile
       const int buf = jj & 1;
@@ -601,7 +760,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         if (alive) mbar_arrive(&bars[B_SEMPTY + buf]);
         if (!first) alive = alive && mbar_wait_warp(&bars[B_OFULL], (jj - 1) & 1, abort);
         if (alive) mbar_arrive(&bars[B_PFULL]);
-        if (last) alive = alive && mbar_wait_warp(&bars[B_OFULL], jj & 1, abort);
+        if (last) alive = alive && mbar_wait_warp(&bars[B_OFULL], jj & 1, abort);   // (no rows: nothing to merge)
         if (named_bar_any(bar_id, 128, !alive)) break;
         continue;
       }
@@ -715,7 +874,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       });
       if (named_bar_any(bar_id, 128, !alive)) break;
       if (last) {
-        const bool complete = split.owner(seg_b, seg_g, 0) == split.owner(seg_b, seg_g, seg_s1 - seg_s0 - 1);
+        const int c0 = split.owner(seg_b, seg_g, 0), c1 = split.owner(seg_b, seg_g, seg_s1 - seg_s0 - 1);
+        const bool complete = c0 == c1;
         const int slot = 2 * blockIdx.x + (seg_s0 < t_begin ? 0 : 1);
         // row owners: 1 / sum, the log2-sum-exp of a piece, and where the row goes
         if (ct < hr) {
@@ -748,6 +908,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
             }
           }
         });
+        if (!complete) arrive_and_merge(c0, c1, rb, hr);
       }
     }
   }
@@ -765,128 +926,6 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   }
 }
 
-// Merge the pieces of segments cut by CTA boundaries, and zero the rows of sequences with no keys.  One CTA per cut
-// segment: all (row, piece) log2-sum-exps are loaded at once, row owners turn them into normalised weights, then
-// each thread accumulates (row, 4 dims) over the pieces with independent loads (two dependent memory rounds in
-// all).  Segments with more than 2048 (row, piece) pairs fall back to one warp per row.
-template <int NP>
-__global__ void __launch_bounds__(256)
-paged_decode_combine(const DecodeParams p, int main_grid) {
-  constexpr int kCombineLse = 2048;
-  __shared__ int prefix[kMaxDecodeSeqs + 1];
-  __shared__ int cprefix[kMaxDecodeSeqs + 1];
-  __shared__ int2 warp_tot[8];
-  __shared__ float lse_s[kCombineLse];   // [rows][pieces]: log2-sum-exp, then normalised weights
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  build_prefix(p, prefix, cprefix, warp_tot, tid, 256);
-  // everything below reads the main kernel's partials or writes the output: wait for that grid to complete
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int KVH = p.num_kv_heads, G = p.group;
-  // zero-length sequences (batch padding): their rows see no key, output 0
-  for (int b = blockIdx.x; b < p.num_seqs; b += gridDim.x) {
-    const SeqShape ss = seq_shape(p, b);
-    if (ss.n >= 1 && ss.n <= p.max_n && ss.L < 1) {
-      const int per_row = p.num_heads * kHeadDim;
-      for (int idx = tid; idx < ss.n * per_row; idx += 256) {
-        const int i = idx / per_row, rem = idx - i * per_row;
-        p.out[(int64_t)(ss.q0 + i) * p.out_row_stride + rem] = __float2bfloat16_rn(0.f);
-      }
-    }
-  }
-  const Split split(prefix, cprefix, p.num_seqs, KVH, main_grid);
-  for (int c = blockIdx.x; c < main_grid; c += gridDim.x) {
-    const int t = split.begin(c);
-    if (c == 0 || t >= split.tiles) continue;
-    const Loc lc = locate(t, prefix, p.num_seqs, KVH);
-    // a cut segment ending in CTA c: it started before c's first tile and its last tile is c's
-    if (lc.s0 >= t || split.owner(lc.b, lc.g, lc.nt - 1) != c) continue;
-    const int c0 = split.owner(lc.b, lc.g, 0);
-    const int pieces = c - c0 + 1;
-    const SeqShape ss = seq_shape(p, lc.b);
-    const int R = ss.n * G;
-    const int64_t out_base = (int64_t)ss.q0 * p.out_row_stride + (int64_t)lc.g * G * kHeadDim;
-    if (R * pieces <= kCombineLse) {
-      // every (row, piece) log2-sum-exp in one round of independent loads
-      for (int idx = tid; idx < R * pieces; idx += 256) {
-        const int r = idx / pieces, pi = idx - r * pieces;
-        const int slot = pi == 0 ? 2 * c0 + 1 : 2 * (c0 + pi);
-        lse_s[idx] = p.part_lse[slot * NP + r];
-      }
-      __syncthreads();
-      // row owners turn them into normalised weights
-      if (tid < R) {
-        float* w = lse_s + tid * pieces;
-        float mx = kNegInf;
-        for (int pi = 0; pi < pieces; ++pi) mx = fmaxf(mx, w[pi]);
-        float den = 0.f;
-        for (int pi = 0; pi < pieces; ++pi) {
-          const float e = (mx == kNegInf || w[pi] == kNegInf) ? 0.f : fast_exp2(w[pi] - mx);
-          w[pi] = e;
-          den += e;
-        }
-        const float inv = den > 0.f ? 1.f / den : 0.f;
-        for (int pi = 0; pi < pieces; ++pi) w[pi] *= inv;
-      }
-      __syncthreads();
-      // (row, 4 dims) per thread; the pieces' loads are independent of each other
-      for (int idx = tid; idx < R * 32; idx += 256) {
-        const int r = idx >> 5, l4 = idx & 31;
-        const float* w = lse_s + r * pieces;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-        for (int pi = 0; pi < pieces; ++pi) {
-          const int slot = pi == 0 ? 2 * c0 + 1 : 2 * (c0 + pi);
-          const float4 v = *reinterpret_cast<const float4*>(p.part_o + ((int64_t)slot * NP + r) * kHeadDim + l4 * 4);
-          const float wp = w[pi];
-          acc.x += wp * v.x;
-          acc.y += wp * v.y;
-          acc.z += wp * v.z;
-          acc.w += wp * v.w;
-        }
-        const int i = r / G, h = r - i * G;
-        uint2 packed;
-        packed.x = pack_bf16x2(acc.x, acc.y);
-        packed.y = pack_bf16x2(acc.z, acc.w);
-        *reinterpret_cast<uint2*>(p.out + out_base + (int64_t)i * p.out_row_stride + h * kHeadDim + l4 * 4) = packed;
-      }
-      __syncthreads();   // lse_s is reused by the next segment
-      continue;
-    }
-    // many pieces: one warp per row, walking the pieces
-    for (int r = warp; r < R; r += 8) {
-      float mx = kNegInf;
-      for (int pi = lane; pi < pieces; pi += 32) {
-        const int slot = pi == 0 ? 2 * c0 + 1 : 2 * (c0 + pi);
-        mx = fmaxf(mx, p.part_lse[slot * NP + r]);
-      }
-      mx = warp_max(mx);
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      float den = 0.f;
-      if (mx != kNegInf) {
-#pragma unroll 4
-        for (int pi = 0; pi < pieces; ++pi) {
-          const int slot = pi == 0 ? 2 * c0 + 1 : 2 * (c0 + pi);
-          const float lse = p.part_lse[slot * NP + r];
-          const float4 v = *reinterpret_cast<const float4*>(p.part_o + ((int64_t)slot * NP + r) * kHeadDim + lane * 4);
-          const float w = lse == kNegInf ? 0.f : fast_exp2(lse - mx);
-          acc.x += w * v.x;
-          acc.y += w * v.y;
-          acc.z += w * v.z;
-          acc.w += w * v.w;
-          den += w;
-        }
-      }
-      const float inv = den > 0.f ? 1.f / den : 0.f;
-      const int i = r / G, h = r - i * G;
-      __nv_bfloat16* dst = p.out + (int64_t)(ss.q0 + i) * p.out_row_stride + (int64_t)(lc.g * G + h) * kHeadDim + lane * 4;
-      uint2 packed;
-      packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-      packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-      *reinterpret_cast<uint2*>(dst) = packed;
-    }
-  }
-}
-
 template <int NP>
 cudaError_t launch_np(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const DecodeParams& p, int grid,
                       cudaStream_t stream) {
@@ -895,21 +934,6 @@ cudaError_t launch_np(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const De
   cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   paged_decode_kernel<NP><<<grid, Cfg<NP>::kThreads, smem, stream>>>(tm_k, tm_v, p);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  // programmatic dependent launch: the combine kernel's launch and prologue overlap the main kernel's tail
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, paged_decode_combine<NP>, p, grid);
-  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -922,8 +946,18 @@ int decode_rows_padded(int rows) {
   return 0;
 }
 
+// Workspace: the merge tickets first, at the same place for every row width and call kind (a workspace shared by
+// several kinds of call keeps them zero between calls), then the partials.
+static size_t ticket_bytes(int grid) { return (2 * static_cast<size_t>(grid) * sizeof(int32_t) + 255) & ~size_t(255); }
+
 size_t decode_workspace_bytes(int grid, int np) {
-  return static_cast<size_t>(2) * grid * np * (kHeadDim + 1) * sizeof(float) + 256;
+  return ticket_bytes(grid) + static_cast<size_t>(2) * grid * np * (kHeadDim + 1) * sizeof(float);
+}
+
+void decode_workspace_layout(void* ws, int grid, int np, DecodeParams* p) {
+  p->counters = static_cast<int32_t*>(ws);
+  p->part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + ticket_bytes(grid));
+  p->part_lse = p->part_o + static_cast<size_t>(2) * grid * np * kHeadDim;
 }
 
 cudaError_t launch_paged_decode(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const DecodeParams& p, int np,

@@ -11,9 +11,10 @@
 // Rules of use (also stated in include/nvattn.h):
 //  - the first call on each device looks up the array's device address with cudaGetSymbolAddress, with that device
 //    current, and caches it; make that first call before any stream capture;
-//  - every call on a device shares the one array and leaves its contents behind; nothing in it has to start at zero
-//    (each partial the combine step reads was written earlier in the same call), but calls that overlap on the GPU
-//    (two streams, say) race on it and must be serialised by the caller;
+//  - every call on a device shares the one array and leaves its contents behind; the only part that must start at
+//    zero (the merge tickets) is cleared by each call itself, in stream order before its kernel, and every partial
+//    a merge reads is written earlier in the same call; calls that overlap on the GPU (two streams, say) race on
+//    the array and must be serialised by the caller;
 //  - a call that needs more than NVA_NOALLOC_SCRATCH_BYTES is rejected with NVA_ERR_WORKSPACE before any launch;
 //  - nothing here allocates: no cudaMalloc, no cudaFree, no allocating library routine.
 #include <cudaTypedefs.h>
@@ -142,8 +143,7 @@ extern "C" NVA_API int nva_paged_decode_noalloc(const void* q, int64_t q_row_str
   p.block_size = block_size;
   p.num_blocks = num_blocks;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
-  p.part_o = static_cast<float*>(scratch);
-  p.part_lse = p.part_o + static_cast<size_t>(2) * grid * np * nva::kHeadDim;
+  nva::decode_workspace_layout(scratch, grid, np, &p);
   const cudaError_t e = nva::launch_paged_decode(tm_k, tm_v, p, np, grid, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? NVA_OK : NVA_ERR_CUDA;
 }

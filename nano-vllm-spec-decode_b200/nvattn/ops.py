@@ -7,9 +7,9 @@
                          causal=True, block_table=)                 flash-attn call at attention.py:67-70
   greedy_accept(target_ids, draft_ids, num_drafts)                  greedy core of verify_drafts, sampler.py:66-82
 
-Every op runs on the caller's current CUDA stream, allocates only its output (and, for attention, a workspace
-from torch's caching allocator, which comes from the graph pool under CUDA-graph capture) and never syncs.
-There is no CPU path: non-CUDA tensors raise.
+Every op runs on the caller's current CUDA stream, allocates only its output and never syncs.  The attention ops
+share one workspace per device (split-KV partials and the merge tickets, see _workspace); there is no CPU path:
+non-CUDA tensors raise.
 """
 import torch
 
@@ -24,6 +24,28 @@ def _need_cuda(*ts):
     for t in ts:
         if t is not None and not t.is_cuda:
             raise ValueError("nvattn ops run on CUDA tensors only (no CPU fallback)")
+
+
+# device index -> the attention workspace in use; earlier (smaller) ones stay referenced because captured CUDA
+# graphs hold their addresses
+_WORKSPACES: dict[int, torch.Tensor] = {}
+_RETIRED: list[torch.Tensor] = []
+
+
+def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """The decode / varlen workspace of a device.  Its merge-ticket words must be zero when a call starts and every
+    call leaves them zero, so it is allocated zero-filled once (grown, zero-filled, when a call needs more) and then
+    reused by every call and every captured graph.  Calls on one device are ordered by the stream they run on:
+    nano-vllm runs attention from one stream; concurrent streams on one device need their own workspaces through
+    the C ABI."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _WORKSPACES.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        if ws is not None:
+            _RETIRED.append(ws)
+        ws = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=device)
+        _WORKSPACES[idx] = ws
+    return ws
 
 
 def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -66,7 +88,7 @@ def flash_attn_with_kvcache(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     ws_bytes = lib.nva_paged_decode_workspace_bytes(B, n, H, KVH, D)
     if ws_bytes == 0:
         raise _lib.NvattnError(f"paged decode does not support q_per_seq={n} with {H // KVH} q heads per kv head")
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    ws = _workspace(ws_bytes, q.device)
     _lib.check(lib.nva_paged_decode(
         q.data_ptr(), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), NB, BS, cache_seqlens.data_ptr(),
         block_table.data_ptr(), block_table.stride(0), B, n, H, KVH, D, float(softmax_scale), out.data_ptr(),
@@ -104,7 +126,7 @@ def flash_attn_varlen_func(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
         kp, kst, vp, vst = k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0)
         kc, vc, bt, bts = 0, 0, 0, 0
     ws_bytes = lib.nva_varlen_workspace_bytes(B, Tq, H, KVH, D)
-    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
+    ws = _workspace(ws_bytes, q.device)
     _lib.check(lib.nva_varlen_attention(
         q.data_ptr(), q.stride(0), kp, kst, vp, vst, kc, vc, NB, BS, cu_seqlens_q.data_ptr(),
         cu_seqlens_k.data_ptr(), B, Tq, Tk, int(max_seqlen_q), int(max_seqlen_k), bt, bts, H, KVH, D,
