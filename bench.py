@@ -16,7 +16,8 @@ value      algorithmic bytes (KV read once per kv head + q + o + the scatter's r
            timed steps by a 256 MiB write outside the events.
 e2e        the same bytes through the public nvattn.attention.Attention.forward with the step's inputs copied
            host->device from pinned memory and the output copied back inside the timed region.
-roofline   the decode launch (main kernel + split combine) timed alone with CUDA events vs measured HBM peak.
+roofline   the decode launch (one kernel: split-KV pieces merged in the same launch) timed alone with CUDA events vs
+           measured HBM peak.
 The reference arm (--impl reference) times the reference semantics (the FP32 torch oracle) on host cores.
 """
 import argparse
@@ -316,7 +317,7 @@ def run_nvattn(args, world, rank, local):
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e_ms, 5),
                 "api": "nvattn.attention.Attention.forward (CUDA-graph replay, inputs H2D from pinned memory, output D2H)"},
-        "roofline": {"kernel": "paged_decode_kernel<16> + paged_decode_combine", "bound": "hbm",
+        "roofline": {"kernel": "paged_decode_kernel<16>", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": pk["hbm"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm"], 4), "peak_source": pk["source"],
                      "traffic": None if traffic is None else round(traffic),

@@ -65,6 +65,10 @@ NVA_API int nva_store_kvcache(const void* key, int64_t key_row_stride, const voi
  * context_lens include the q_per_seq new tokens (already stored by nva_store_kvcache).  A sequence with
  * context length 0 (batch padding) reads nothing and gets a zero output.  q_per_seq * (H / KVH) <= 48.
  * Requires head_dim 128, bf16, block_size a multiple of 128.  workspace >= nva_paged_decode_workspace_bytes().
+ * Workspace contract: zero-fill it once before its first use (cudaMemset); every call leaves its first 256-byte
+ * aligned block of merge tickets at zero again, so the same workspace serves every later call in stream order (also
+ * nva_varlen_attention calls, and captured CUDA graphs).  Calls that may overlap on one device (different streams)
+ * need separate workspaces.
  */
 NVA_API int nva_paged_decode(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,
                              int32_t num_blocks, int32_t block_size, const int32_t* context_lens,
@@ -84,7 +88,8 @@ NVA_API size_t nva_paged_decode_workspace_bytes(int32_t num_seqs, int32_t q_per_
  * Keys/values come from the paged cache through block_tables when block_tables != NULL (prefix cache,
  * chunked prefill, mixed batches), else from the contiguous key/value tensors at rows cu_seqlens_k[b] + pos.
  * max_seqlen_q / max_seqlen_k are upper bounds only (they size nothing on the device).
- * Requires head_dim 128, bf16.  workspace >= nva_varlen_workspace_bytes().
+ * Requires head_dim 128, bf16.  workspace >= nva_varlen_workspace_bytes(); same zero-filled-once contract as
+ * nva_paged_decode's (the two may share one workspace).
  */
 NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void* key, int64_t key_row_stride,
                                  const void* value, int64_t value_row_stride, const void* k_cache,

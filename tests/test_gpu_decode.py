@@ -53,7 +53,8 @@ def test_decode_config2_full(cuda):
 
 
 def test_decode_long_single_sequence_splits(cuda):
-    """One 4096-token sequence: its 8 kv-head segments are cut across many CTAs and merged by the combine."""
+    """One 4096-token sequence: its 8 kv-head segments are cut across many CTAs (more than 16 pieces each) and
+    merged in the kernel."""
     b = batch([4096], NB=32, seed=5)
     assert_attn_close(run_decode(b), ref_decode(b), "split")
 
