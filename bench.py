@@ -13,7 +13,7 @@ only NCCL calls are the barrier and the max-over-ranks of the timings.
 
 value      algorithmic bytes (KV read once per kv head + q + o + the scatter's read and write) of all ranks,
            divided by the slowest rank's device time (CUDA events), inputs resident in HBM, L2 flushed between
-           timed steps by a 256 MiB write outside the events.
+           timed steps outside the events (a 256 MiB write, then a 256 MiB read that writes the dirty lines back).
 e2e        the same bytes through the public nvattn.attention.Attention.forward with the step's inputs copied
            host->device from pinned memory and the output copied back inside the timed region.
 roofline   the decode launch (one kernel: split-KV pieces merged in the same launch) timed alone with CUDA events vs
@@ -178,17 +178,31 @@ def capture(fn):
     return g
 
 
+class L2Flush:
+    """Flushes the 126 MB L2 between timed steps, outside the events: a 256 MiB write, then a read of another
+    256 MiB buffer, which evicts the written (dirty) lines and writes them back before the step starts, so the timed
+    step neither finds its inputs in L2 nor pays for someone else's write-backs."""
+
+    def __init__(self):
+        self.w = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        self.r = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def __call__(self):
+        self.w.zero_()
+        torch.count_nonzero(self.r)
+
+
 def time_steps(fn, steps, warmup, flush):
-    """Per-step device time (ms) with CUDA events on the current stream; L2 flushed before each step outside the
-    events.  Returns the list of step times."""
+    """Per-step device time (ms) with CUDA events on the current stream; L2 flushed (`flush()`) before each step
+    outside the events.  Returns the list of step times."""
     for _ in range(warmup):
-        flush.zero_()
+        flush()
         fn()
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for i in range(steps):
-        flush.zero_()
+        flush()
         starts[i].record()
         fn()
         ends[i].record()
@@ -205,7 +219,7 @@ def run_nvattn(args, world, rank, local):
     B = b.num_seqs
     q4 = b.q.view(B, 1, H, 128)
     out = torch.empty_like(q4)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = L2Flush()
     a_bytes = attn_bytes(lens, 1, H, KVH)
     s_bytes = scatter_bytes(B, KVH)
 
@@ -313,7 +327,8 @@ def run_nvattn(args, world, rank, local):
                    "timing": "CUDA-graph replay per step, CUDA events, max over ranks",
                    "global_batch": B, "per_rank_q_heads": H, "per_rank_kv_heads": KVH, "head_dim": 128,
                    "block_size": 256, "context": "U[512, 4096]", "parallelism": f"kv-head shards x{world}",
-                   "l2": "flushed between timed steps (256 MiB write outside the events)"},
+                   "l2": "flushed between timed steps outside the events: 256 MiB write, then a 256 MiB read that "
+                         "writes the dirty lines back"},
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e_ms, 5),
                 "api": "nvattn.attention.Attention.forward (CUDA-graph replay, inputs H2D from pinned memory, output D2H)"},

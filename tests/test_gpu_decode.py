@@ -158,3 +158,29 @@ def test_kernels_match_flash_attn_golden(cuda, name):
                                          max_seqlen_k=b.max_seqlen_k, cu_seqlens_k=b.cu_seqlens_k,
                                          softmax_scale=b.scale, causal=True, block_table=bt)
     assert_attn_close(got, fa2_out.float(), f"kernels vs flash-attn: {name}")
+
+
+@pytest.mark.parametrize("pieces_case", ["two_pieces", "table", "many_pieces"])
+def test_merge_tickets_left_zero_and_repeatable(cuda, pieces_case):
+    """The workspace contract: the merge tickets (first block of the workspace) are zero again after every call,
+    whichever merge path ran (two pieces, the weight table for 3..16 pieces, the plain loop beyond), and repeated
+    calls sharing the workspace give bitwise identical outputs.  A varlen call in between shares the workspace."""
+    from nvattn import ops
+    from nvattn.workloads import varlen_batch
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    ticket_bytes = (2 * sms * 4 + 255) // 256 * 256
+    lens = {"two_pieces": [1500] * 40, "table": [2048 * 3] * 4, "many_pieces": [4096]}[pieces_case]
+    b = batch(lens, n=3 if pieces_case == "two_pieces" else 1, NB=512, seed=21)
+    first = run_decode(b).clone()
+    ws = ops._WORKSPACES[torch.cuda.current_device()]
+    torch.cuda.synchronize()
+    assert int(ws[:ticket_bytes].count_nonzero()) == 0, "tickets not left at zero"
+    v = varlen_batch([1, 3, 200], [300, 40, 900], 32, 8, 128, 64, 0.5, 3, device="cuda")
+    ops.flash_attn_varlen_func(v.q, v.k_cache, v.v_cache, max_seqlen_q=v.max_seqlen_q, cu_seqlens_q=v.cu_seqlens_q,
+                               max_seqlen_k=v.max_seqlen_k, cu_seqlens_k=v.cu_seqlens_k, softmax_scale=v.scale,
+                               causal=True, block_table=v.block_tables)
+    torch.cuda.synchronize()
+    assert int(ws[:ticket_bytes].count_nonzero()) == 0, "tickets not zero after a varlen call"
+    again = run_decode(b)
+    assert torch.equal(first, again)
+    assert_attn_close(again, ref_decode(b), f"tickets {pieces_case}")
