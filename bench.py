@@ -337,7 +337,7 @@ def run_nvattn(args, world, rank, local):
                      "frac": round(achieved / pk["hbm"], 4), "peak_source": pk["source"],
                      "traffic": None if traffic is None else round(traffic),
                      "algorithmic_bytes": round(a_bytes), "us": round(k_ms * 1e3, 2)},
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 2 * args.steps,   # per timed headline step: store_kvcache_kernel + paged_decode_kernel
         "secondary": secondary,
     }
     clocks = clk.summary()
