@@ -43,7 +43,10 @@ constexpr uint32_t kFull = 0xffffffffu;
 // warps, so an entry is never rewritten before the softmax warps have read it.
 constexpr int kInfoRing = 8;
 
-constexpr int kMergePieces = 16;   // pieces of a cut segment merged through the shared weight table
+constexpr int kMergePieces = 16;
+// Row maxima move only when a score passes them by more than this (log2 units): until then P <= 2^8, exact enough in
+// bf16 and in the FP32 sums.
+constexpr float kRescaleLog2 = 8.0f;   // pieces of a cut segment merged through the shared weight table
 
 template <int NP>
 struct Cfg {
@@ -702,6 +705,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     float l[NPH], o[NPH], s[NPH];
     int R = 0, nr = 8, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0, seg_b = 0;
     bool alive = true;
+    bool rescaled_prev = false;               // whether the previous tile moved some row maxima (alpha != 1)
     // A piece of a cut segment is done (this group's rows [rb, rb + hr) written): take the group's ticket for the
     // segment; the group that brings it to the number of pieces merges those rows of all pieces and puts the
     // counter back to zero, so the counters are zero again when the launch ends (the workspace contract).  Every
@@ -764,8 +768,12 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         if (named_bar_any(bar_id, 128, !alive)) break;
         continue;
       }
-      // ---- S tile -> masked, scaled scores; per-warp column maxima
+      // ---- S tile -> masked, scaled scores.  Row maxima are lazy: scores are scaled by each row's m_s, and the
+      // exact tile maxima are taken (per-warp column maxima -> row owners) only when some score exceeds its row's
+      // m_s by more than 2^kRescaleLog2 (always at a segment's first tile); otherwise alpha = 1 and the reduction
+      // and two barriers are skipped.  P stays below 2^kRescaleLog2 either way.
       alive = alive && mbar_wait_warp(&bars[B_SFULL + buf], (jj >> 1) & 1, abort);
+      bool need = first;
       if (alive) {
         tc_fence_after();
         // query i of the segment sees tokens <= L - n + i, i.e. row r = i*G + h is visible iff r >= G*(tok-L+n)
@@ -781,25 +789,42 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
             const int r = rb + i;
             s[i] = (r >= rmin && r < R) ? s[i] * p.scale_log2 : kNegInf;
           }
-          warp_columns<HR, true>(s, red + (buf * 4 + wq) * NP + rb, lane);
+          if (!first) {
+            const float* ms = m_s + rb;
+#pragma unroll
+            for (int r = 0; r < HR; r += 4) {
+              const float4 m4 = *reinterpret_cast<const float4*>(ms + r);
+              need |= (s[r] > m4.x + kRescaleLog2) | (s[r + 1] > m4.y + kRescaleLog2) |
+                      (s[r + 2] > m4.z + kRescaleLog2) | (s[r + 3] > m4.w + kRescaleLog2);
+            }
+          }
         });
       }
-      if (named_bar_any(bar_id, 128, !alive)) break;
-      // ---- running max (one owner thread per row) and rescale factor
-      if (ct < hr) {
-        const int row = rb + ct;
-        float mn = 0.f, alpha = 1.f;
-        if (row < R) {
-          const float* rr = red + buf * 4 * NP;
-          const float tm = fmaxf(fmaxf(rr[row], rr[NP + row]), fmaxf(rr[2 * NP + row], rr[3 * NP + row]));
-          const float mo = first ? kNegInf : m_s[row];
-          mn = fmaxf(mo, tm);
-          alpha = (mn == kNegInf) ? 1.f : fast_exp2(mo - mn);
+      // one vote per tile; a warp that gave up votes too and is caught by the second vote below
+      const bool rescale = named_bar_any(bar_id, 128, need || !alive);
+      if (rescale) {
+        if (named_bar_any(bar_id, 128, !alive)) break;
+        with_rows<NP>(nr, [&](auto nr_c) {
+          constexpr int HR = group_rows<NP, decltype(nr_c)::value>();
+          warp_columns<HR, true>(s, red + (buf * 4 + wq) * NP + rb, lane);
+        });
+        named_bar_sync(bar_id, 128);
+        // row owners: the maximum moves only for rows whose tile maximum passed it by more than the threshold
+        if (ct < hr) {
+          const int row = rb + ct;
+          float mn = 0.f, alpha = 1.f;
+          if (row < R) {
+            const float* rr = red + buf * 4 * NP;
+            const float tm = fmaxf(fmaxf(rr[row], rr[NP + row]), fmaxf(rr[2 * NP + row], rr[3 * NP + row]));
+            const float mo = first ? kNegInf : m_s[row];
+            mn = (first || tm > mo + kRescaleLog2) ? fmaxf(mo, tm) : mo;
+            alpha = (mo == kNegInf || mn == mo) ? 1.f : fast_exp2(mo - mn);
+          }
+          m_s[row] = mn;
+          alpha_s[buf * NP + row] = alpha;
         }
-        m_s[row] = mn;
-        alpha_s[buf * NP + row] = alpha;
+        named_bar_sync(bar_id, 128);
       }
-      named_bar_sync(bar_id, 128);
       with_rows<NP>(nr, [&](auto nr_c) {
         constexpr int HR = group_rows<NP, decltype(nr_c)::value>();
         const float* ms = m_s + rb;
@@ -807,8 +832,15 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
 #pragma unroll
         for (int r = 0; r < HR; r += 4) {
           const float4 m4 = *reinterpret_cast<const float4*>(ms + r);
-          const float4 a4 = *reinterpret_cast<const float4*>(al + r);
-          const float mv[4] = {m4.x, m4.y, m4.z, m4.w}, av[4] = {a4.x, a4.y, a4.z, a4.w};
+          const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+          float av[4] = {1.f, 1.f, 1.f, 1.f};
+          if (rescale) {
+            const float4 a4 = *reinterpret_cast<const float4*>(al + r);
+            av[0] = a4.x;
+            av[1] = a4.y;
+            av[2] = a4.z;
+            av[3] = a4.w;
+          }
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const float pr = (s[r + i] == kNegInf) ? 0.f : fast_exp2(s[r + i] - mv[i]);
@@ -824,8 +856,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
             const float* ap = alpha_s + (buf ^ 1) * NP + rb;
             float ot[HR];
             tmem_ld_cols<HR>(t_lane + 2 * NP + rb, ot);
+            if (rescaled_prev) {
 #pragma unroll
-            for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
+              for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
+            } else {
+#pragma unroll
+              for (int i = 0; i < HR; ++i) o[i] += ot[i];
+            }
             tc_fence_before();
           }
         }
@@ -865,13 +902,19 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
             const float* ap = alpha_s + buf * NP + rb;
             float ot[HR];
             tmem_ld_cols<HR>(t_lane + 2 * NP + rb, ot);
+            if (rescale) {
 #pragma unroll
-            for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
+              for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
+            } else {
+#pragma unroll
+              for (int i = 0; i < HR; ++i) o[i] += ot[i];
+            }
             tc_fence_before();
             warp_columns<HR, false>(l, lred + wq * NP + rb, lane);
           }
         }
       });
+      rescaled_prev = rescale;
       if (named_bar_any(bar_id, 128, !alive)) break;
       if (last) {
         const int c0 = split.owner(seg_b, seg_g, 0), c1 = split.owner(seg_b, seg_g, seg_s1 - seg_s0 - 1);
