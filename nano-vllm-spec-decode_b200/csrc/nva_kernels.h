@@ -37,7 +37,7 @@ struct DecodeParams {
   float scale_log2;
   float* part_o;     // [2 * grid, NP, 128] split partial outputs (normalised)
   float* part_lse;   // [2 * grid, NP] their log2-sum-exp
-  int32_t* counters; // [grid][2] merge tickets per cut segment (CTA of its first piece) and softmax group: zero on
+  int32_t* counters; // [grid][4] merge tickets per cut segment (CTA of its first piece) and softmax group: zero on
                      // entry and on exit
 };
 

@@ -44,13 +44,16 @@ constexpr uint32_t kFull = 0xffffffffu;
 constexpr int kInfoRing = 8;
 
 constexpr int kMergePieces = 16;
+constexpr int kTicketStride = 4;   // merge tickets per CTA: one per softmax warpgroup (at most 3)
 // Row maxima move only when a score passes them by more than this (log2 units): until then P <= 2^8, exact enough in
 // bf16 and in the FP32 sums.
 constexpr float kRescaleLog2 = 8.0f;   // pieces of a cut segment merged through the shared weight table
 
 template <int NP>
 struct Cfg {
-  static constexpr int kWG = NP >= 32 ? 2 : 1;                   // softmax warpgroups (row halves)
+  // softmax warpgroups (row shares): two at 32/48 rows.  Three at 48 rows measured 69 vs 72 us on verify k = 8 but
+  // 216 vs 210 us on config 4's mixed step (short segments leave two groups idle; 128 registers a thread spill)
+  static constexpr int kWG = NP >= 32 ? 2 : 1;
   static constexpr int kThreads = kConsumerBase + 128 * kWG;
   static constexpr int kRowsPerGroup = NP / kWG;                 // per-thread row arrays
   // Ring depths: 3 tiles; 2 for the 32/48-row tiles, whose softmax needs longer per tile than HBM does and whose
@@ -316,11 +319,16 @@ __device__ __forceinline__ bool umma_lane(int lane) {
   }
 }
 
-// Rows a softmax warpgroup carries for an NR-wide tile: all of them with one group; with two, half (at least one
-// 8-row P^T vector each, so an 8-row tile gives the second group 8 padding rows).
+// Rows each of `wg_count` softmax warpgroups carries for an NR-wide tile: all NR with one group; otherwise NR split
+// into equal shares rounded up to whole 8-row P^T vectors (8, 16 or 24 rows); groups past NR hold padding only.
+__host__ __device__ constexpr int group_rows_rt(int wg_count, int nr) {
+  return wg_count == 1 ? nr : nr <= 8 ? 8 : ((nr + wg_count - 1) / wg_count + 7) / 8 * 8;
+}
+
+// The same at compile time, for the kernel's group count.
 template <int NP, int NR>
 __device__ __forceinline__ constexpr int group_rows() {
-  return Cfg<NP>::kWG == 1 ? NR : (NR < 16 ? 8 : NR / 2);
+  return group_rows_rt(Cfg<NP>::kWG, NR);
 }
 
 // HR consecutive TMEM columns (8, 16 or 24) of this warp's lanes, one wait.
@@ -714,7 +722,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       named_bar_sync(bar_id, 128);
       bool last_arrival = false;
       if (ct == 0) {
-        int32_t* ticket = p.counters + 2 * c0 + wg;
+        int32_t* ticket = p.counters + kTicketStride * c0 + wg;
         __threadfence();   // release: the group's partial rows (ordered before by the barrier) before the ticket
         last_arrival = atomicAdd(ticket, 1) == c1 - c0;
         if (last_arrival) {
@@ -752,11 +760,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           o[r] = 0.f;
         }
       }
-      const int hr = C::kWG == 1 ? nr : (nr < 16 ? 8 : nr / 2);   // group_rows at run time
+      const int hr = group_rows_rt(C::kWG, nr);
       const int rb = wg * hr;
       const int tok0 = inf.z * kTileTokens;
       const int tok = tok0 + ct;
-      if (C::kWG == 2 && rb >= R) {
+      if (C::kWG > 1 && rb >= R) {
         // every row of this group is padding (a short segment): only keep the S / P / O phases paced.  SEMPTY of
         // tile jj is given after S(jj) exists, PFULL of jj after PV(jj-1) finished, as the working group does, so
         // no arrival can land in a phase that the other group has not reached.
@@ -991,7 +999,9 @@ int decode_rows_padded(int rows) {
 
 // Workspace: the merge tickets first, at the same place for every row width and call kind (a workspace shared by
 // several kinds of call keeps them zero between calls), then the partials.
-static size_t ticket_bytes(int grid) { return (2 * static_cast<size_t>(grid) * sizeof(int32_t) + 255) & ~size_t(255); }
+static size_t ticket_bytes(int grid) {
+  return (kTicketStride * static_cast<size_t>(grid) * sizeof(int32_t) + 255) & ~size_t(255);
+}
 
 size_t decode_workspace_bytes(int grid, int np) {
   return ticket_bytes(grid) + static_cast<size_t>(2) * grid * np * (kHeadDim + 1) * sizeof(float);
