@@ -12,9 +12,9 @@
 //  - the first call on each device looks up the array's device address with cudaGetSymbolAddress, with that device
 //    current, and caches it; make that first call before any stream capture;
 //  - every call on a device shares the one array and leaves its contents behind; the only part that must start at
-//    zero (the merge tickets) is cleared by each call itself, in stream order before its kernel, and every partial
-//    a merge reads is written earlier in the same call; calls that overlap on the GPU (two streams, say) race on
-//    the array and must be serialised by the caller;
+//    zero (the merge tickets) is cleared by each call itself with a memset in stream order before its kernel, and
+//    every partial a merge reads is written earlier in the same call; calls that overlap on the GPU (two streams,
+//    say) race on the array and must be serialised by the caller;
 //  - a call that needs more than NVA_NOALLOC_SCRATCH_BYTES is rejected with NVA_ERR_WORKSPACE before any launch;
 //  - nothing here allocates: no cudaMalloc, no cudaFree, no allocating library routine.
 #include <cudaTypedefs.h>
@@ -144,6 +144,12 @@ extern "C" NVA_API int nva_paged_decode_noalloc(const void* q, int64_t q_row_str
   p.num_blocks = num_blocks;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   nva::decode_workspace_layout(scratch, grid, np, &p);
-  const cudaError_t e = nva::launch_paged_decode(tm_k, tm_v, p, np, grid, static_cast<cudaStream_t>(stream));
+  // The merge tickets at the start of the array must be zero when the kernel starts.  A normal call leaves them
+  // zero, but one that gave up part-way may not have, so every call clears them first, in stream order (a memset
+  // of the existing array: nothing is allocated).
+  const size_t ticket_bytes =
+      static_cast<size_t>(reinterpret_cast<unsigned char*>(p.part_o) - reinterpret_cast<unsigned char*>(p.counters));
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, ticket_bytes, static_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) e = nva::launch_paged_decode(tm_k, tm_v, p, np, grid, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? NVA_OK : NVA_ERR_CUDA;
 }
