@@ -18,7 +18,8 @@
 //
 // Warp roles (256 threads; 384 for the 32/48-row instantiations):
 //   0 = K producer, 3 = V producer: block-table ids prefetched 32 tiles at a time, then TMA 64 dims x 128 tokens
-//       boxes into 3-stage rings; K slots are released right after S = K Q^T, V slots after the PV product;
+//       boxes into 3-stage rings; K slots are released right after S = K Q^T, V slots after the PV product.  They
+//       start before the TMEM allocation and leave when done; the other warps meet on named barrier 3;
 //   1 = TMEM owner + UMMA issuer: polls the ring / softmax barriers and issues whichever product is ready;
 //   2 = Q loader: gathers a segment's rows into the swizzled operand layout (cp.async, zero-filled padding);
 //   4..7 (and 8..11) = softmax: thread ct of a warpgroup owns TMEM lane ct (token ct of S^T, dim ct of O^T).
@@ -85,7 +86,8 @@ struct Cfg {
 
 enum {
   B_KFULL = 0, B_KEMPTY = 3, B_VFULL = 6, B_VEMPTY = 9, B_SFULL = 12, B_SEMPTY = 14, B_PFULL = 16, B_OFULL = 17,
-  B_QFULL = 18, B_QEMPTY = 20, B_INFO = 22   // B_INFO + kInfoRing <= 32
+  B_QFULL = 18, B_QEMPTY = 20, B_INFO = 22,   // B_INFO + kInfoRing <= B_KSTART
+  B_KSTART = 30   // the K producer has issued its first tile (the V producer starts after it)
 };
 
 struct SeqShape {
@@ -116,8 +118,9 @@ __device__ __forceinline__ int seq_tiles(const DecodeParams& p, int b) {
 }
 
 // Cost of a (sequence, kv head) segment in the work split, in tile units: its tiles plus this much for the segment's
-// start and end (Q load, first-tile latency, final PV, normalisation, output), measured on B200 at about two tiles.
-constexpr int kSegCost = 2;
+// start and end (Q load, first-tile latency, final PV, normalisation, output, a merge).  Fitted on B200 from per-CTA
+// finish times at 1.8 (decode) to 3 (verify) tiles; 3 measured best on verify and mixed steps and neutral on decode.
+constexpr int kSegCost = 3;
 
 // Exclusive prefix sums over the sequences, per kv head: prefix[b] = tiles before sequence b, cprefix[b] = cost units
 // before it (tiles + kSegCost per non-empty segment; padding sequences add nothing).  Called by all `nthreads`
@@ -515,6 +518,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     mbar_init(&bars[B_PFULL], 128 * C::kWG);
     mbar_init(&bars[B_OFULL], 1);
     for (int i = 0; i < kInfoRing; ++i) mbar_init(&bars[B_INFO + i], 1);
+    mbar_init(&bars[B_KSTART], 1);
     *abort = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -539,23 +543,18 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   const int t_end = split.begin(blockIdx.x + 1);
   const int ntiles = t_end > t_begin ? t_end - t_begin : 0;
   if (ntiles == 0) return;   // nothing for this CTA (e.g. a varlen batch without short runs): no TMEM, no pipeline
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
-    tmem_relinquish();
-  }
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if ((warp == 0 || warp == 3) && ntiles > 0) {
+  if (warp == 0 || warp == 3) {
     // ------------------------------------------------------------ K (warp 0) and V (warp 3) producers
+    // They need no TMEM and start streaming at once; they leave when their tiles are issued (the other warps wait
+    // for every tile, so the block outlives the copies).  K goes first: the V producer starts after the first K tile
+    // is issued, so that across the GPU the first S products are not queued behind V tiles needed later.
     const bool is_k = warp == 0;
     const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
     uint8_t* ring = smem + (is_k ? C::kK : C::kV);
     uint64_t* full = bars + (is_k ? B_KFULL : B_VFULL);
     uint64_t* empty = bars + (is_k ? B_KEMPTY : B_VEMPTY);
     const int stages = is_k ? C::kKStages : C::kVStages;
-    bool stop = false;
+    bool stop = !is_k && !mbar_wait_warp(&bars[B_KSTART], 0, abort);
     for (int base = 0; base < ntiles && !stop; base += 32) {
       // lane-parallel descriptors of the next 32 tiles (the block-table reads overlap each other)
       int g = 0, j = 0, b = 0, row0 = 0, flags = 0, n = 0, L = 0, q0 = 0, nt = 0;
@@ -604,11 +603,23 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           uint8_t* dst = ring + st * kTileBytes;
           tma_load_3d(dst, tm, 0, gi, ri, &full[st]);
           tma_load_3d(dst + kSlab, tm, 64, gi, ri, &full[st]);
+          if (is_k && jj == 0) mbar_arrive(&bars[B_KSTART]);
         }
         __syncwarp();
       }
     }
-  } else if (warp == 1 && ntiles > 0) {
+    return;
+  }
+  // ------------------------------------------------------------ the other warps: TMEM, then their roles
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  named_bar_sync(3, C::kThreads - 64);
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 1 && ntiles > 0) {
     // ------------------------------------------------------------ UMMA issuer (whole warp polls, an elected lane issues)
     const uint64_t q_desc0 = umma_desc_sw128(smem_u32(smem + C::kQ), 16, 1024);
     const uint64_t k_desc0 = umma_desc_sw128(smem_u32(smem + C::kK), 16, 1024);
@@ -964,12 +975,12 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     }
   }
 
-  __syncthreads();
+  named_bar_sync(3, C::kThreads - 64);
   if (*abort) {
     // a wait gave up: let any copy or MMA still in flight land before the shared memory and TMEM go away
-    if (tid == 0) atomicOr(&g_error_word, kErrTimeout);
+    if (tid == kConsumerBase) atomicOr(&g_error_word, kErrTimeout);
     for (int i = 0; i < 1000; ++i) sleep_ns(1000);
-    __syncthreads();
+    named_bar_sync(3, C::kThreads - 64);
   }
   if (warp == 1) {
     tc_fence_after();
