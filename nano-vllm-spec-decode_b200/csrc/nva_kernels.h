@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <utility>
 
 namespace nva {
 
@@ -39,14 +40,35 @@ struct DecodeParams {
   float* part_lse;   // [2 * grid, NP] their log2-sum-exp
   int32_t* counters; // [grid][4] merge tickets per cut segment (CTA of its first piece) and softmax group: zero on
                      // entry and on exit
+  int32_t pdl;       // 1: launched with a programmatic dependency on the preceding kernel (launch_paged_decode sets it)
 };
 
 size_t decode_workspace_bytes(int grid, int np);
 // Carve the workspace (decode_workspace_bytes(grid, np) bytes) into the partials and the merge counters.
 void decode_workspace_layout(void* ws, int grid, int np, DecodeParams* p);
 int decode_rows_padded(int rows);  // 16, 32 or 48 (0 if too many)
+// pdl: launch with a programmatic dependency on the preceding kernel in the stream (the kernel's blocks may start
+// while it finishes; they wait for it before their first global read, and only then let the next such grid start).
+// Only for a preceding kernel, not a memset or copy.
 cudaError_t launch_paged_decode(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const DecodeParams& p, int np,
-                                int grid, cudaStream_t stream);
+                                int grid, cudaStream_t stream, bool pdl);
+
+// Launch helper: `kernel` with a programmatic dependency on the preceding kernel when `pdl`, else a plain launch.
+template <class... KArgs, class... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Varlen prefill kernel (long query runs) — q rows tiled by 128 per (sequence, q head).
 struct PrefillParams {
@@ -67,11 +89,18 @@ struct PrefillParams {
   int32_t num_blocks;
   int32_t q_tiles_bound;        // capacity of the work plan: an upper bound on the number of 128-row q tiles
   int32_t o_tma;                // 1: full output tiles are written by TMA stores through the output tensor map
+  int32_t wait_primary;         // 1: the preceding kernel (the plan kernel) produced data this grid reads
   float scale_log2;
   int32_t* plan;                // workspace: [0] = number of q tiles, [1..] = (seq << 12 | q tile), heaviest first,
                                 // [1 + q_tiles_bound] = work counter (items taken after the first wave)
 };
 constexpr int kMaxPrefillTiles = 4096;
+// The prefill work plan (one block), launched with a programmatic dependency on the preceding kernel.
+cudaError_t launch_prefill_plan(const PrefillParams& p, cudaStream_t stream);
+// The prefill kernel, launched with a programmatic dependency on the preceding kernel: the plan kernel
+// (p.wait_primary = 1: it waits for the plan before reading it) or the decode kernel of the same call, which comes
+// after the plan kernel and has waited for it (p.wait_primary = 0: its blocks may run beside the decode kernel's
+// last blocks).  Either way the grid completes only after the preceding one has.
 cudaError_t launch_prefill(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                            const CUtensorMap& tm_o, const PrefillParams& p, int grid, cudaStream_t stream);
 

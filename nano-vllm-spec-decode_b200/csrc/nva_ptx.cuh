@@ -14,6 +14,15 @@ extern __device__ uint32_t g_error_word;
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s: far above any launch of these kernels
 
+// Programmatic dependent launch.  griddep_wait: wait until the grid this one was launched after (with a programmatic
+// dependency) has completed and its memory is visible; returns at once without such a dependency.
+// griddep_launch_dependents: the next grid launched with a programmatic dependency on this one may start its blocks
+// once every block of this grid has called it or exited (their own griddep_wait still waits for this grid).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

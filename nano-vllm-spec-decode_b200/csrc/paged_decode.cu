@@ -525,6 +525,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
   }
+  // With a programmatic dependency on the preceding kernel (the prefill plan of a varlen call): everything above ran
+  // beside its end; wait for it before the first global read, then let the next grid (the call's prefill kernel)
+  // start its blocks.
+  if (p.pdl) {
+    griddep_wait();
+    if (tid == 0) griddep_launch_dependents();
+  }
   build_prefix(p, prefix, cprefix, warp_tot, tid, C::kThreads);   // ends with __syncthreads
   // sequences whose query rows see no key (length 0: batch padding) get zero rows, from CTA b % grid
   for (int b = blockIdx.x; b < p.num_seqs; b += gridDim.x) {
@@ -990,13 +997,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
 
 template <int NP>
 cudaError_t launch_np(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const DecodeParams& p, int grid,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, bool pdl) {
   constexpr int smem = Cfg<NP>::kBytes;
   static_assert(smem <= 232448, "shared memory budget");
   cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  paged_decode_kernel<NP><<<grid, Cfg<NP>::kThreads, smem, stream>>>(tm_k, tm_v, p);
-  return cudaGetLastError();
+  return launch_kernel(paged_decode_kernel<NP>, dim3(grid), dim3(Cfg<NP>::kThreads), smem, stream, pdl, tm_k, tm_v,
+                       p);
 }
 
 }  // namespace
@@ -1024,12 +1031,14 @@ void decode_workspace_layout(void* ws, int grid, int np, DecodeParams* p) {
   p->part_lse = p->part_o + static_cast<size_t>(2) * grid * np * kHeadDim;
 }
 
-cudaError_t launch_paged_decode(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const DecodeParams& p, int np,
-                                int grid, cudaStream_t stream) {
+cudaError_t launch_paged_decode(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const DecodeParams& params,
+                                int np, int grid, cudaStream_t stream, bool pdl) {
+  DecodeParams p = params;
+  p.pdl = pdl ? 1 : 0;
   switch (np) {
-    case 16: return launch_np<16>(tm_k, tm_v, p, grid, stream);
-    case 32: return launch_np<32>(tm_k, tm_v, p, grid, stream);
-    case 48: return launch_np<48>(tm_k, tm_v, p, grid, stream);
+    case 16: return launch_np<16>(tm_k, tm_v, p, grid, stream, pdl);
+    case 32: return launch_np<32>(tm_k, tm_v, p, grid, stream, pdl);
+    case 48: return launch_np<48>(tm_k, tm_v, p, grid, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -150,6 +150,8 @@ extern "C" NVA_API int nva_paged_decode_noalloc(const void* q, int64_t q_row_str
   const size_t ticket_bytes =
       static_cast<size_t>(reinterpret_cast<unsigned char*>(p.part_o) - reinterpret_cast<unsigned char*>(p.counters));
   cudaError_t e = cudaMemsetAsync(p.counters, 0, ticket_bytes, static_cast<cudaStream_t>(stream));
-  if (e == cudaSuccess) e = nva::launch_paged_decode(tm_k, tm_v, p, np, grid, static_cast<cudaStream_t>(stream));
+  // (a plain launch: the operation before the kernel is the memset, not a kernel)
+  if (e == cudaSuccess)
+    e = nva::launch_paged_decode(tm_k, tm_v, p, np, grid, static_cast<cudaStream_t>(stream), false);
   return e == cudaSuccess ? NVA_OK : NVA_ERR_CUDA;
 }

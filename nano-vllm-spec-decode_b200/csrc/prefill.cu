@@ -92,6 +92,10 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(const PrefillParams 
   __shared__ int code[kMaxPrefillTiles];
   __shared__ int warp_tot[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // launched with a programmatic dependency: the preceding kernel (or the last call's prefill kernel, which may
+  // still read the plan) completes before the plan is rewritten; then the call's next kernel may start its blocks
+  griddep_wait();
+  if (tid == 0) griddep_launch_dependents();
   // tiles per sequence and their exclusive prefix (B <= 1024: one element per thread)
   int nt = 0, n = 0, L = 0;
   if (tid < p.num_seqs) {
@@ -191,6 +195,11 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched with a programmatic dependency on the preceding kernel.  After the plan kernel (wait_primary) the plan
+  // is read only once that grid has completed; after the decode kernel of the same call (which waited for the plan
+  // kernel before letting this grid start) nothing here depends on it, and the blocks run beside its last blocks.
+  if (p.wait_primary) griddep_wait();
+  if (tid == 0) griddep_launch_dependents();
   const int total = p.plan[0];
 
   if (warp == 0 || warp == 3) {
@@ -568,20 +577,24 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  // the grid completes only after the preceding one has (a later grid that waits for this one can rely on both)
+  griddep_wait();
 }
 
 }  // namespace
 
+cudaError_t launch_prefill_plan(const PrefillParams& p, cudaStream_t stream) {
+  if (p.num_seqs > kMaxDecodeSeqs || p.q_tiles_bound > kMaxPrefillTiles) return cudaErrorInvalidValue;
+  return launch_kernel(prefill_plan_kernel, dim3(1), dim3(1024), 0, stream, true, p);
+}
+
 cudaError_t launch_prefill(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                            const CUtensorMap& tm_o, const PrefillParams& p, int grid, cudaStream_t stream) {
   if (p.num_seqs > kMaxDecodeSeqs || p.q_tiles_bound > kMaxPrefillTiles) return cudaErrorInvalidValue;
-  prefill_plan_kernel<<<1, 1024, 0, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  const cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (e != cudaSuccess) return e;
-  prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, tm_o, p);
-  return cudaGetLastError();
+  return launch_kernel(prefill_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, true, tm_q, tm_k, tm_v, tm_o,
+                       p);
 }
 
 }  // namespace nva
