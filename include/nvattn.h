@@ -90,6 +90,10 @@ NVA_API size_t nva_paged_decode_workspace_bytes(int32_t num_seqs, int32_t q_per_
  * max_seqlen_q / max_seqlen_k are upper bounds only (they size nothing on the device).
  * Requires head_dim 128, bf16.  workspace >= nva_varlen_workspace_bytes(); same zero-filled-once contract as
  * nva_paged_decode's (the two may share one workspace).
+ * The call enqueues up to three kernels on `stream` (the prefill work plan, the decode kernel for query runs of up
+ * to 48 / group tokens, the prefill kernel for longer runs), each launched with a programmatic dependency on the one
+ * before.  Together they keep the order of a single kernel: the first waits for the preceding work in the stream
+ * before it touches memory, and the last completes only after the others.
  */
 NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void* key, int64_t key_row_stride,
                                  const void* value, int64_t value_row_stride, const void* k_cache,
