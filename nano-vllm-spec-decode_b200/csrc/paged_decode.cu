@@ -62,12 +62,16 @@ struct Cfg {
   static constexpr int kKStages = NP >= 32 ? 2 : 3;
   static constexpr int kVStages = NP >= 32 ? 2 : 3;
   static constexpr int kQBuf = 2;                                // Q double buffer: next segment's rows load early
+  // P^T / O buffers: two at 32/48 rows, so a tile's P is handed to the tensor pipe before the previous tile's O is
+  // folded (verify k = 8 69.6 -> 65.5 us, mixed step 186 -> 181 us); one at 16 rows, where HBM sets the pace
+  static constexpr int kPBuf = NP >= 32 ? 2 : 1;
   static constexpr int kK = 0;                                   // K ring
   static constexpr int kV = kKStages * kTileBytes;               // V ring
   static constexpr int kQ = (kKStages + kVStages) * kTileBytes;  // Q buffers, NP * 256 bytes each
-  static constexpr int kP = kQ + kQBuf * NP * 256;               // P^T, NP * 256 bytes
-  static constexpr int kBars = kP + NP * 256;                    // 32 x u64
-  static constexpr int kInfo = kBars + 32 * 8;                   // kInfoRing x 2 x int4
+  static constexpr int kP = kQ + kQBuf * NP * 256;               // [kPBuf] P^T, NP * 256 bytes each
+  static constexpr int kBarCount = kPBuf == 2 ? 33 : 31;         // mbarriers (the B_* enum)
+  static constexpr int kBars = kP + kPBuf * NP * 256;            // kBarCount x u64
+  static constexpr int kInfo = kBars + (kBarCount * 8 + 15) / 16 * 16;   // kInfoRing x 2 x int4
   static constexpr int kRed = kInfo + kInfoRing * 32;            // [2][4][NP] column maxima per warp
   static constexpr int kM = kRed + 2 * 4 * NP * 4;               // [NP] running max
   static constexpr int kAlpha = kM + NP * 4;                     // [2][NP] rescale factors
@@ -84,11 +88,18 @@ struct Cfg {
   static constexpr int kBytes = kEnd + 1024;                     // + slack for 1024-byte alignment
 };
 
+// S is double buffered by tile parity (S(j) in buffer j & 1); P and O by tile parity when Cfg::kPBuf = 2 (P(j) and
+// O(j) = P(j) V(j) in buffer j & 1), else single (buffer 0).  The barriers of P / O buffer b: pfull_bar(b),
+// ofull_bar(b) (buffer 1's come last, so one-buffer instantiations keep a 31-barrier area).
 enum {
   B_KFULL = 0, B_KEMPTY = 3, B_VFULL = 6, B_VEMPTY = 9, B_SFULL = 12, B_SEMPTY = 14, B_PFULL = 16, B_OFULL = 17,
   B_QFULL = 18, B_QEMPTY = 20, B_INFO = 22,   // B_INFO + kInfoRing <= B_KSTART
-  B_KSTART = 30   // the K producer has issued its first tile (the V producer starts after it)
+  B_KSTART = 30,  // the K producer has issued its first tile (the V producer starts after it)
+  B_PFULL1 = 31, B_OFULL1 = 32
 };
+static_assert(B_PFULL1 - B_PFULL == B_OFULL1 - B_OFULL, "buffer 1's barriers at one distance");
+__device__ __forceinline__ int pfull_bar(int b) { return B_PFULL + b * (B_PFULL1 - B_PFULL); }
+__device__ __forceinline__ int ofull_bar(int b) { return B_OFULL + b * (B_OFULL1 - B_OFULL); }
 
 struct SeqShape {
   int n;   // query rows
@@ -477,6 +488,9 @@ __global__ void __launch_bounds__(Cfg<NP>::kThreads, 1)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const DecodeParams p) {
   using C = Cfg<NP>;
+  // P / O buffer of tile t and the phase parity of its barriers
+  auto pbuf = [](int t) { return C::kPBuf == 2 ? (t & 1) : 0; };
+  auto pphase = [](int t) { return C::kPBuf == 2 ? ((t >> 1) & 1) : (t & 1); };
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBars);
@@ -515,8 +529,10 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       mbar_init(&bars[B_QFULL + i], 32);
       mbar_init(&bars[B_QEMPTY + i], 1);
     }
-    mbar_init(&bars[B_PFULL], 128 * C::kWG);
-    mbar_init(&bars[B_OFULL], 1);
+    for (int i = 0; i < C::kPBuf; ++i) {
+      mbar_init(&bars[pfull_bar(i)], 128 * C::kWG);
+      mbar_init(&bars[ofull_bar(i)], 1);
+    }
     for (int i = 0; i < kInfoRing; ++i) mbar_init(&bars[B_INFO + i], 1);
     mbar_init(&bars[B_KSTART], 1);
     *abort = 0;
@@ -668,7 +684,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     issue_qk();
     while (ok && pv < ntiles) {
       const int st = pv % C::kVStages;
-      if (!mbar_wait_warp(&bars[B_PFULL], pv & 1, abort)) break;
+      const int pb = pbuf(pv);   // P / O buffer of this tile
+      if (!mbar_wait_warp(&bars[pfull_bar(pb)], pphase(pv), abort)) break;
       if (!mbar_wait_warp(&bars[B_VFULL + st], (pv / C::kVStages) & 1, abort)) break;
       const uint32_t idesc_pv =
           umma_idesc_bf16(128, min(NP, mma_width(info[2 * (pv % kInfoRing) + 1].x * G)), true, true);
@@ -678,8 +695,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         // B = P^T: 16 tokens per step (two 8-token core-matrix groups, LBO 128; 8-row groups, SBO 2048) -> +256 B
         constexpr uint32_t kOffV[8] = {0, 128, 256, 384, 512, 640, 768, 896};
         constexpr uint32_t kOffP[8] = {0, 16, 32, 48, 64, 80, 96, 112};
-        umma_bf16_ss_x8(tmem + 2 * NP, v_desc0 + ((st * kTileBytes) >> 4), p_desc0, idesc_pv, 0u, kOffV, kOffP);
-        umma_commit(&bars[B_OFULL]);
+        umma_bf16_ss_x8(tmem + (2 + pb) * NP, v_desc0 + ((st * kTileBytes) >> 4), p_desc0 + ((pb * NP * 256) >> 4),
+                        idesc_pv, 0u, kOffV, kOffP);
+        umma_commit(&bars[ofull_bar(pb)]);
         umma_commit(&bars[B_VEMPTY + st]);
       }
       __syncwarp();
@@ -783,14 +801,14 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       const int tok0 = inf.z * kTileTokens;
       const int tok = tok0 + ct;
       if (C::kWG > 1 && rb >= R) {
-        // every row of this group is padding (a short segment): only keep the S / P / O phases paced.  SEMPTY of
-        // tile jj is given after S(jj) exists, PFULL of jj after PV(jj-1) finished, as the working group does, so
-        // no arrival can land in a phase that the other group has not reached.
+        // every row of this group is padding (a short segment): only keep the S / P phases paced.  SEMPTY of
+        // tile jj is given after S(jj) exists and PFULL of jj after PV(jj-2) (the buffer's last product) finished,
+        // as the working group does, so no arrival can land in a phase that the other group has not reached.
         alive = alive && mbar_wait_warp(&bars[B_SFULL + buf], (jj >> 1) & 1, abort);
         if (alive) mbar_arrive(&bars[B_SEMPTY + buf]);
-        if (!first) alive = alive && mbar_wait_warp(&bars[B_OFULL], (jj - 1) & 1, abort);
-        if (alive) mbar_arrive(&bars[B_PFULL]);
-        if (last) alive = alive && mbar_wait_warp(&bars[B_OFULL], jj & 1, abort);   // (no rows: nothing to merge)
+        // (two groups: always two P / O buffers)
+        if (jj >= 2) alive = alive && mbar_wait_warp(&bars[ofull_bar(pbuf(jj))], pphase(jj - 2), abort);
+        if (alive) mbar_arrive(&bars[pfull_bar(pbuf(jj))]);
         if (named_bar_any(bar_id, 128, !alive)) break;
         continue;
       }
@@ -874,24 +892,27 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
             s[r + i] = pr;
           }
         }
-        // ---- fold the previous tile's O; PV of tile jj-1 must also be done before P is overwritten
-        if (!first) {
-          alive = mbar_wait_warp(&bars[B_OFULL], (jj - 1) & 1, abort);
-          if (alive) {
-            tc_fence_after();
-            const float* ap = alpha_s + (buf ^ 1) * NP + rb;
-            float ot[HR];
-            tmem_ld_cols<HR>(t_lane + 2 * NP + rb, ot);
-            if (rescaled_prev) {
+        // ---- fold the previous tile's O
+        auto fold_prev = [&]() {
+          if (!first && alive) {
+            alive = mbar_wait_warp(&bars[ofull_bar(pbuf(jj - 1))], pphase(jj - 1), abort);
+            if (alive) {
+              tc_fence_after();
+              const float* ap = alpha_s + (buf ^ 1) * NP + rb;
+              float ot[HR];
+              tmem_ld_cols<HR>(t_lane + (2 + pbuf(jj - 1)) * NP + rb, ot);
+              if (rescaled_prev) {
 #pragma unroll
-              for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
-            } else {
+                for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
+              } else {
 #pragma unroll
-              for (int i = 0; i < HR; ++i) o[i] += ot[i];
+                for (int i = 0; i < HR; ++i) o[i] += ot[i];
+              }
+              tc_fence_before();
             }
-            tc_fence_before();
           }
-        }
+        };
+        if constexpr (C::kPBuf == 1) fold_prev();   // one P buffer: PV(jj-1) must finish before P is rewritten
         // ---- rows past the sequence end may hold stale or uninitialised values: zero V there so P = 0 cannot
         // meet a NaN in the PV product (last tile of a sequence; group 0, before its P arrival)
         if (alive && wg == 0 && L - tok0 < kTileTokens) {
@@ -905,10 +926,12 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
             }
           }
         }
-        // ---- P^T (bf16), MN-major without swizzle: 8 consecutive rows of token ct form one 16-byte vector.
-        // Rows past NR (up to the UMMA N) are never read back: their O^T columns are ignored.
+        // ---- P^T (bf16) into its buffer, MN-major without swizzle: 8 consecutive rows of token ct form one 16-byte
+        // vector.  Rows past NR (up to the UMMA N) are never read back: their O^T columns are ignored.  The buffer's
+        // last reader has finished: its O was folded before this point (PV(jj-1) just above with one buffer;
+        // PV(jj-2) at tile jj-1 or at the end of its segment with two).
         if (alive) {
-          uint8_t* pb = p_smem + ct * 16 + (rb >> 3) * 2048;
+          uint8_t* pb = p_smem + pbuf(jj) * NP * 256 + ct * 16 + (rb >> 3) * 2048;
 #pragma unroll
           for (int m = 0; m < HR / 8; ++m) {
             uint4 v;
@@ -919,15 +942,16 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
             *reinterpret_cast<uint4*>(pb + m * 2048) = v;
           }
           fence_proxy_async_smem();
-          mbar_arrive(&bars[B_PFULL]);
+          mbar_arrive(&bars[pfull_bar(pbuf(jj))]);
         }
+        if constexpr (C::kPBuf == 2) fold_prev();   // the fold waits for PV(jj-1) after this tile's P is handed off
         if (last && alive) {
-          alive = mbar_wait_warp(&bars[B_OFULL], jj & 1, abort);
+          alive = mbar_wait_warp(&bars[ofull_bar(pbuf(jj))], pphase(jj), abort);
           if (alive) {
             tc_fence_after();
             const float* ap = alpha_s + buf * NP + rb;
             float ot[HR];
-            tmem_ld_cols<HR>(t_lane + 2 * NP + rb, ot);
+            tmem_ld_cols<HR>(t_lane + (2 + pbuf(jj)) * NP + rb, ot);
             if (rescale) {
 #pragma unroll
               for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
