@@ -1,0 +1,76 @@
+"""Long CUDA-graph replay runs of the full-size decode (config 2), verify (config 3, k = 8) and mixed (config 4)
+steps, as nano-vllm replays its captured steps: every replay must finish without any bounded wait giving up (the
+device error word stays 0) and give bitwise the same output as the eager call (the kernels are deterministic:
+the split, the merge order and each item's arithmetic depend only on the inputs).  Timing-dependent races between
+the kernels' warp roles, or between the chained kernels of a varlen call, would show up here as a set error bit or
+a changed output."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+REPLAYS = 300
+
+
+def _capture(fn):
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def _decode_call(b, out):
+    from nvattn import ops
+    n = b.q_per_seq
+    q = b.q.view(b.num_seqs, n, b.q.shape[1], b.q.shape[2])
+
+    def call():
+        ops.flash_attn_with_kvcache(q, b.k_cache, b.v_cache, cache_seqlens=b.context_lens,
+                                    block_table=b.block_tables, softmax_scale=b.scale, out=out)
+    return call
+
+
+def _varlen_call(b, out):
+    from nvattn import ops
+
+    def call():
+        ops.flash_attn_varlen_func(b.q, b.k_cache, b.v_cache, max_seqlen_q=b.max_seqlen_q,
+                                   cu_seqlens_q=b.cu_seqlens_q, max_seqlen_k=b.max_seqlen_k,
+                                   cu_seqlens_k=b.cu_seqlens_k, softmax_scale=b.scale, causal=True,
+                                   block_table=b.block_tables, out=out)
+    return call
+
+
+@pytest.mark.parametrize("case", ["decode_config2", "verify_config3_k8", "mixed_config4"])
+def test_graph_replays_stay_clean_and_bitwise_stable(cuda, case):
+    from nvattn import _lib
+    from nvattn.workloads import decode_config, mixed_config, verify_config
+    if case == "mixed_config4":
+        b = mixed_config(seed=0, device="cuda")
+        out = torch.empty_like(b.q)
+        call = _varlen_call(b, out)
+    else:
+        b = (decode_config(seed=0, device="cuda", device_fill=True) if case == "decode_config2"
+             else verify_config(8, seed=0, device="cuda", device_fill=True))
+        out = torch.empty(b.num_seqs, b.q_per_seq, b.q.shape[1], b.q.shape[2], dtype=b.q.dtype, device=cuda)
+        call = _decode_call(b, out)
+    _lib.clear_device_error()
+    call()
+    torch.cuda.synchronize()
+    ref = out.clone()
+    assert _lib.device_error() == 0
+    g = _capture(call)
+    for i in range(REPLAYS):
+        out.fill_(float("nan"))
+        g.replay()
+        if i % 50 == 49 or i == REPLAYS - 1:
+            torch.cuda.synchronize()
+            assert _lib.device_error() == 0, f"a bounded wait gave up by replay {i}"
+            assert torch.equal(out, ref), f"replay {i} differs from the eager call"
+    g.reset()
