@@ -1033,7 +1033,9 @@ cudaError_t launch_np(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const De
 }  // namespace
 
 int decode_rows_padded(int rows) {
-  if (rows <= 16) return 16;
+  // 9-16 rows take the 32-row instantiation, whose two softmax groups split them 8 + 8 (the 16-row one has a
+  // single group)
+  if (rows <= 8) return 16;
   if (rows <= 32) return 32;
   if (rows <= 48) return 48;
   return 0;
