@@ -518,13 +518,16 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           tmem_st32(t_lane + st * 128 + 32 * wg, pk);
           const float2 s01 = fadd2(fadd2(sum4[0], sum4[1]), fadd2(sum4[2], sum4[3]));
           l += s01.x + s01.y;
-          tc_fence_before();
-          mbar_arrive(&bars[B_PFULL]);
-          // keep the PV completions observed in order (never more than one behind)
+          // Observe PV(g-1) before handing over P(g), so that at most one PV product is ever unobserved: otherwise
+          // P(g+1) could complete the PFULL phase after P(g) before the issuer saw P(g)'s (its parity wait would
+          // then wait for a phase that needs PV(g) itself), and PV(g) could complete ODONE before this wait for
+          // PV(g-1) (the same two-phase aliasing).
           if (pv_seen < g) {
             alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
             pv_seen = g;
           }
+          tc_fence_before();
+          if (alive) mbar_arrive(&bars[B_PFULL]);
         }
       }
       // ---- epilogue: O / l.  The two half-row sums meet in TMEM columns 384/385; O is staged in the item's idle
