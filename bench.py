@@ -356,7 +356,8 @@ def prefill_flops(q_lens, k_lens, H, D=128):
 
 def varlen_rows(world, rank, args, flush, pk):
     """BASELINE config 4 rows at this rank's head shard: the prefill chunks alone (paged prefix, tensor-core bound),
-    a 2048-token prefill without prefix (contiguous K/V), and the whole mixed step (decode rows HBM-bound)."""
+    a 2048-token prefill without prefix (contiguous K/V), sixteen 1024-token prompts (config 5's prompt shape), and
+    the whole mixed step (decode rows HBM-bound)."""
     from nvattn import ops
     from nvattn.workloads import mixed_config, varlen_batch
     H, KVH = 32 // world, 8 // world
@@ -388,6 +389,15 @@ def varlen_rows(world, rank, args, flush, pk):
     fl = prefill_flops(lens, lens, H)
     rows["prefill_4x512_contiguous"] = {"us": round(ms * 1e3, 2), "TFLOPs": round(world * fl / (ms * 1e-3) / 1e12, 1),
                                         "frac_bf16": round(fl / (ms * 1e-3) / 1e12 / pk["bf16"], 3)}
+    del b
+    # the prompt shape of BASELINE config 5 (1024-token prompts), 16 of them in one prefill step
+    lens = [1024] * 16
+    b = varlen_batch(lens, lens, H, KVH, 128, 64, 0.5, args.seed + 42, device="cuda", paged=False)
+    ms = timed(b, False)
+    fl = prefill_flops(lens, lens, H)
+    rows["prefill_16x1024_contiguous"] = {"us": round(ms * 1e3, 2),
+                                          "TFLOPs": round(world * fl / (ms * 1e-3) / 1e12, 1),
+                                          "frac_bf16": round(fl / (ms * 1e-3) / 1e12 / pk["bf16"], 3)}
     del b
     b = mixed_config(seed=args.seed, device="cuda", num_heads=H, num_kv_heads=KVH)
     ms = timed(b, True)
