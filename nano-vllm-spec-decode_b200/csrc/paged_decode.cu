@@ -18,9 +18,11 @@
 //
 // Warp roles (256 threads; 384 for the 32/48-row instantiations):
 //   0 = K producer, 3 = V producer: block-table ids prefetched 32 tiles at a time, then TMA 64 dims x 128 tokens
-//       boxes into 3-stage rings; K slots are released right after S = K Q^T, V slots after the PV product.  They
-//       start before the TMEM allocation and leave when done; the other warps meet on named barrier 3;
-//   1 = TMEM owner + UMMA issuer: polls the ring / softmax barriers and issues whichever product is ready;
+//       boxes into rings (3 stages at 16 rows, 2 at 32/48); K slots are released right after S = K Q^T, V slots
+//       after the PV product.  They start before the TMEM allocation and leave when done; the other warps meet on
+//       named barrier 3;
+//   1 = TMEM owner + UMMA issuer: products in a fixed order, QK(0), QK(1), then PV(j), QK(j+2), ... (S, P and O
+//       buffers are reused by tile parity, so this order is what keeps every barrier within one phase);
 //   2 = Q loader: gathers a segment's rows into the swizzled operand layout (cp.async, zero-filled padding);
 //   4..7 (and 8..11) = softmax: thread ct of a warpgroup owns TMEM lane ct (token ct of S^T, dim ct of O^T).
 //       Column maxima and sums over the 128 tokens use a transposed butterfly (each shuffle stage halves the rows
@@ -234,12 +236,6 @@ __device__ __forceinline__ Loc locate(int t, const int* prefix, int B, int KVH) 
   l.j = rem - l.g * l.nt;
   l.s0 = KVH * prefix[lo] + l.g * l.nt;
   return l;
-}
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
-  return v;
 }
 
 // Transposed butterfly over the 32 lanes of a warp for NR (power of two <= 32) columns held by every lane: each
