@@ -532,15 +532,20 @@ def profile_case(args):
             chunks, prefixes = [512, 640, 640], [0, 256, 1024]
             b = varlen_batch(chunks, [c + p for c, p in zip(chunks, prefixes)], 32, 8, 128, 64, 0.5, args.seed + 40,
                              device="cuda")
+        elif case == "prefill16k":
+            lens = [1024] * 16
+            b = varlen_batch(lens, lens, 32, 8, 128, 64, 0.5, args.seed + 42, device="cuda", paged=False)
         else:
             b = mixed_config(seed=args.seed, device="cuda")
         out = torch.empty_like(b.q)
+        paged = b.meta.get("paged", True)
+        kk, vv, bt = (b.k_cache, b.v_cache, b.block_tables) if paged else (b.k_new, b.v_new, None)
 
         def call():
-            ops.flash_attn_varlen_func(b.q, b.k_cache, b.v_cache, max_seqlen_q=b.max_seqlen_q,
+            ops.flash_attn_varlen_func(b.q, kk, vv, max_seqlen_q=b.max_seqlen_q,
                                        cu_seqlens_q=b.cu_seqlens_q, max_seqlen_k=b.max_seqlen_k,
                                        cu_seqlens_k=b.cu_seqlens_k, softmax_scale=b.scale, causal=True,
-                                       block_table=b.block_tables, out=out)
+                                       block_table=bt, out=out)
     for _ in range(args.warmup):
         call()
     torch.cuda.synchronize()
@@ -563,7 +568,7 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile-case", choices=["decode", "verify8", "prefill4", "mixed4"],
+    ap.add_argument("--profile-case", choices=["decode", "verify8", "prefill4", "prefill16k", "mixed4"],
                     help="run one workload --steps times on one GPU (for ncu captures) and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
