@@ -1,5 +1,5 @@
 """Long CUDA-graph replay runs of the full-size decode (config 2), verify (config 3, k = 8) and mixed (config 4)
-steps, as nano-vllm replays its captured steps: every replay must finish without any bounded wait giving up (the
+steps and of a prefill of sixteen 1024-token prompts, as nano-vllm replays its captured steps: every replay must finish without any bounded wait giving up (the
 device error word stays 0) and give bitwise the same output as the eager call (the kernels are deterministic:
 the split, the merge order and each item's arithmetic depend only on the inputs).  Timing-dependent races between
 the kernels' warp roles, or between the chained kernels of a varlen call, would show up here as a set error bit or
@@ -38,21 +38,23 @@ def _decode_call(b, out):
 
 def _varlen_call(b, out):
     from nvattn import ops
+    paged = b.meta.get("paged", True)
+    k, v, bt = (b.k_cache, b.v_cache, b.block_tables) if paged else (b.k_new, b.v_new, None)
 
     def call():
-        ops.flash_attn_varlen_func(b.q, b.k_cache, b.v_cache, max_seqlen_q=b.max_seqlen_q,
-                                   cu_seqlens_q=b.cu_seqlens_q, max_seqlen_k=b.max_seqlen_k,
-                                   cu_seqlens_k=b.cu_seqlens_k, softmax_scale=b.scale, causal=True,
-                                   block_table=b.block_tables, out=out)
+        ops.flash_attn_varlen_func(b.q, k, v, max_seqlen_q=b.max_seqlen_q, cu_seqlens_q=b.cu_seqlens_q,
+                                   max_seqlen_k=b.max_seqlen_k, cu_seqlens_k=b.cu_seqlens_k, softmax_scale=b.scale,
+                                   causal=True, block_table=bt, out=out)
     return call
 
 
-@pytest.mark.parametrize("case", ["decode_config2", "verify_config3_k8", "mixed_config4"])
+@pytest.mark.parametrize("case", ["decode_config2", "verify_config3_k8", "mixed_config4", "prefill_16x1024"])
 def test_graph_replays_stay_clean_and_bitwise_stable(cuda, case):
     from nvattn import _lib
-    from nvattn.workloads import decode_config, mixed_config, verify_config
-    if case == "mixed_config4":
-        b = mixed_config(seed=0, device="cuda")
+    from nvattn.workloads import decode_config, mixed_config, varlen_batch, verify_config
+    if case in ("mixed_config4", "prefill_16x1024"):
+        b = (mixed_config(seed=0, device="cuda") if case == "mixed_config4"
+             else varlen_batch([1024] * 16, [1024] * 16, 32, 8, 128, 64, 0.5, 42, device="cuda", paged=False))
         out = torch.empty_like(b.q)
         call = _varlen_call(b, out)
     else:
