@@ -84,6 +84,10 @@ def flash_attn_with_kvcache(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     assert block_table.dtype == torch.int32 and block_table.stride(-1) == 1 and block_table.shape[0] == B
     if out is None:
         out = torch.empty(B, n, H, D, dtype=q.dtype, device=q.device)
+    else:   # rows are addressed as (b * n + i) * out.stride(1): the same layout rules as q
+        _need_cuda(out)
+        assert out.dtype == q.dtype and out.shape == q.shape and out.device == q.device
+        assert out.stride(-1) == 1 and out.stride(2) == D and out.stride(0) == n * out.stride(1)
     lib = _lib.load()
     ws_bytes = lib.nva_paged_decode_workspace_bytes(B, n, H, KVH, D)
     if ws_bytes == 0:
@@ -112,6 +116,10 @@ def flash_attn_varlen_func(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ma
     B = cu_seqlens_q.numel() - 1
     if out is None:
         out = torch.empty(Tq, H, D, dtype=q.dtype, device=q.device)
+    else:
+        _need_cuda(out)
+        assert out.dtype == q.dtype and out.shape == q.shape and out.device == q.device
+        assert out.stride(-1) == 1 and out.stride(1) == D
     lib = _lib.load()
     if block_table is not None:
         NB, BS, KVH, _ = k.shape
