@@ -79,6 +79,23 @@ def test_accept_matches_reference_golden(cuda, case, dtype):
     assert n.cpu().tolist() == c["next_token"].tolist()
 
 
+@pytest.mark.parametrize("case", sorted(ACCEPT))
+def test_verify_drafts_greedy_matches_reference_golden(cuda, case):
+    """The golden cases came from the reference's verify_drafts fed one-hot logits whose argmax is the target id;
+    the same logits (bf16, as the LM head gives them) go through nvattn.sampler.verify_drafts_greedy."""
+    from nvattn.sampler import verify_drafts_greedy
+    c = ACCEPT[case]
+    t = torch.from_numpy(c["target"]).cuda()
+    S, K1 = t.shape
+    logits = torch.zeros(S * K1, max(int(t.max()) + 1, 2), dtype=torch.bfloat16, device=cuda)
+    logits.scatter_(1, t.reshape(-1, 1), 1.0)
+    d = torch.from_numpy(c["drafts"]).reshape(S, K1 - 1).cuda()
+    a, n = verify_drafts_greedy(logits, d, torch.from_numpy(c["num_drafts"]).cuda())
+    assert a.dtype == n.dtype == torch.int64
+    assert a.cpu().tolist() == c["num_accepted"].tolist()
+    assert n.cpu().tolist() == c["next_token"].tolist()
+
+
 @pytest.mark.parametrize("k", [1, 2, 4, 8])
 def test_accept_config3_large_batch(cuda, k):
     """Config 3 shape at 512 // (1+k) sequences (the largest verify batch, config.py:69-73)."""

@@ -167,3 +167,13 @@ def test_greedy_accept_without_drafts_passes_null(rec):
     (name, a), = rec.calls
     assert name == "nva_greedy_accept" and a[2] == a[3] == 0 and a[6] == 0 and a[7] == 8
     assert acc.dtype == nxt.dtype == torch.int64 and acc.shape == nxt.shape == (4,)
+
+
+def test_verify_drafts_greedy_hands_int64_argmax_ids_to_accept(rec):
+    from nvattn.sampler import verify_drafts_greedy
+    S, K, V = 3, 2, 11
+    logits = torch.zeros(S * (K + 1), V, dtype=torch.bfloat16)
+    acc, nxt = verify_drafts_greedy(logits, torch.zeros(S, K, dtype=torch.int32), torch.full((S,), K))
+    (name, a), = rec.calls
+    assert name == "nva_greedy_accept" and (a[5], a[6], a[7]) == (S, K, 8)
+    assert acc.dtype == nxt.dtype == torch.int64 and acc.shape == (S,)
