@@ -260,10 +260,13 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
   nva::PrefillParams pp{};
   CUtensorMap tm_q, tm_o;
   bool o_tma = false;
+  // Work items of two query tiles (prefill_pair_kernel) share each K / V tile between two softmax groups, faster per
+  // tile, but halve the number of items: chosen when the call's rows x heads give at least four such items per SM.
+  const bool pair = static_cast<int64_t>(total_q) * num_heads >= 4LL * grid * 256;
   if (long_runs) {
     if ((rc = encode_rows(&tm_q, q, num_heads, total_q, q_row_stride * 2)) != NVA_OK) return rc;
-    // full 128-row output tiles leave through TMA stores when the output rows allow a tensor map
-    o_tma = aligned16(out) && (out_row_stride * 2) % 16 == 0;
+    // single-tile kernel: full 128-row output tiles leave through TMA stores when the output rows allow a tensor map
+    o_tma = !pair && aligned16(out) && (out_row_stride * 2) % 16 == 0;
     if (o_tma && (rc = encode_rows(&tm_o, out, num_heads, total_q, out_row_stride * 2)) != NVA_OK) return rc;
     pp.q = static_cast<const __nv_bfloat16*>(q);
     pp.q_row_stride = q_row_stride;
@@ -281,6 +284,7 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
     pp.block_size = block_size;
     pp.num_blocks = num_blocks;
     pp.q_tiles_bound = cap;
+    pp.tiles_per_item = pair ? 2 : 1;
     pp.o_tma = o_tma ? 1 : 0;
     pp.wait_primary = paged ? 0 : 1;   // after the decode kernel / directly after the plan kernel
     pp.scale_log2 = softmax_scale * 1.4426950408889634f;
@@ -314,7 +318,8 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
   }
   if (long_runs) {
     const int pgrid = static_cast<int>(std::min<int64_t>(grid, static_cast<int64_t>(cap) * num_heads));
-    cudaError_t e = nva::launch_prefill(tm_q, tm_k, tm_v, o_tma ? tm_o : tm_q, pp, pgrid, s);
+    cudaError_t e = pair ? nva::launch_prefill_pair(tm_q, tm_k, tm_v, pp, pgrid, s)
+                         : nva::launch_prefill(tm_q, tm_k, tm_v, o_tma ? tm_o : tm_q, pp, pgrid, s);
     if (e != cudaSuccess) return cuda_fail(e);
   }
   return NVA_OK;

@@ -88,13 +88,24 @@ struct PrefillParams {
   int32_t block_size;
   int32_t num_blocks;
   int32_t q_tiles_bound;        // capacity of the work plan: an upper bound on the number of 128-row q tiles
+  int32_t tiles_per_item;       // 128-row q tiles per work item: 1 (prefill_kernel) or 2 (prefill_pair_kernel)
   int32_t o_tma;                // 1: full output tiles are written by TMA stores through the output tensor map
   int32_t wait_primary;         // 1: the preceding kernel (the plan kernel) produced data this grid reads
   float scale_log2;
-  int32_t* plan;                // workspace: [0] = number of q tiles, [1..] = (seq << 12 | q tile), heaviest first,
-                                // [1 + q_tiles_bound] = work counter (items taken after the first wave)
+  int32_t* plan;                // workspace: [0] = number of items, [1..] = (seq << 12 | item of the sequence),
+                                // heaviest first, [1 + q_tiles_bound] = work counter (items taken after the first
+                                // wave)
 };
 constexpr int kMaxPrefillTiles = 4096;
+
+// Key tiles visible to 128-row query tile qt of a sequence with n queries and L keys, causal bottom-right: at least
+// one (a fully masked tile keeps the pipeline uniform; those rows get a zero output), 0 past the last query tile.
+__host__ __device__ __forceinline__ int prefill_tile_nkv(int n, int L, int qt) {
+  const int rows = n - qt * 128 < 128 ? n - qt * 128 : 128;
+  if (rows <= 0) return 0;
+  const int t = (L - n + qt * 128 + rows - 1) / 128 + 1;
+  return t > 1 ? t : 1;
+}
 // The prefill work plan (one block), launched with a programmatic dependency on the preceding kernel.
 cudaError_t launch_prefill_plan(const PrefillParams& p, cudaStream_t stream);
 // The prefill kernel, launched with a programmatic dependency on the preceding kernel: the plan kernel
@@ -103,6 +114,10 @@ cudaError_t launch_prefill_plan(const PrefillParams& p, cudaStream_t stream);
 // last blocks).  Either way the grid completes only after the preceding one has.
 cudaError_t launch_prefill(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                            const CUtensorMap& tm_o, const PrefillParams& p, int grid, cudaStream_t stream);
+// The same step with work items of two consecutive query tiles (p.tiles_per_item = 2 in the plan): one softmax
+// warpgroup per tile, sharing each K / V tile.  Same launch contract as launch_prefill.
+cudaError_t launch_prefill_pair(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                                const PrefillParams& p, int grid, cudaStream_t stream);
 
 cudaError_t launch_store_kvcache(const void* key, int64_t key_row_stride, const void* value,
                                  int64_t value_row_stride, void* k_cache, void* v_cache, int64_t num_slots,

@@ -1,17 +1,17 @@
 // Varlen causal prefill attention for sm_100a (replaces flash_attn_varlen_func at nanovllm/layers/attention.py:67-70
 // for query runs longer than the decode kernel's 48-row tile: prefill chunks, with or without a paged prefix).
 //
-// Work item = (128-row query tile of one sequence, q head).  A one-CTA plan kernel lists the query tiles heaviest
-// first (most key tiles under the causal mask); persistent CTAs take the first wave by block index and every later
-// item from an atomic counter (longest-processing-time-first list scheduling), so the long tiles start first and
-// the short ones fill in wherever a CTA frees up.
+// Work item = (128-row query tile of one sequence, q head).  A one-CTA plan kernel (also used by prefill_pair.cu,
+// whose items are two tiles) lists the items heaviest first (most key tiles under the causal mask); persistent CTAs
+// take the first wave by block index and every later item from an atomic counter (longest-processing-time-first
+// list scheduling), so the long tiles start first and the short ones fill in wherever a CTA frees up.
 //
 // Per item: S = Q K^T with M = 128 query rows on the TMEM lanes, N = 128 keys (A = Q, B = K tile, both K-major
 // 128B-swizzled straight from TMA); P = exp2(S * scale - m) in bf16, written back into the first 64 columns of its
 // own S buffer in tensor memory; O += P V in TMEM (A = P read from TMEM, B = V tile, MN-major, straight from TMA).
-// Keeping P out of shared memory pays for a 3-stage V ring.  One thread owns one query row: its maximum and sum
-// are thread-local (no shuffles, no barriers between the softmax warps).  O is rescaled in TMEM only when a row's
-// maximum grows by more than 2^8 (until then P values up to 256 are exact enough in bf16 and FP32 sums).
+// Keeping P out of shared memory pays for a 3-stage V ring.  Each query row is shared by two threads, one per
+// key half (see the warp roles below).  O is rescaled in TMEM only when a row's maximum grows by more than 2^8
+// (until then P values up to 256 are exact enough in bf16 and FP32 sums).
 //
 // Warp roles (384 threads): 0 = Q + K producer (also publishes the item descriptors), 3 = V producer, 1 = TMEM owner
 // + UMMA issuer, 2 = output writer, 4..11 = softmax + epilogue in two warpgroups: thread (group w, row t) owns keys
@@ -77,16 +77,15 @@ __device__ __forceinline__ Item load_item(const PrefillParams& p, int k, int tot
   it.k0 = __ldg(p.cu_k + it.b);
   it.L = __ldg(p.cu_k + it.b + 1) - it.k0;
   it.rows = min(128, it.n - it.qt * 128);
-  const int last_row = it.qt * 128 + it.rows - 1;
-  // keys [0, L - n + last_row] are visible to the tile; at least one (fully masked) tile keeps the pipeline
-  // uniform when no key is visible (those rows get a zero output)
-  it.nkv = max(1, (it.L - it.n + last_row) / 128 + 1);
+  it.nkv = prefill_tile_nkv(it.n, it.L, it.qt);
   return it;
 }
 
 // ------------------------------------------------------------------------------------------------ plan kernel
-// plan[0] = number of query tiles of sequences with q_len >= min_q; plan[1 + i] = (seq << 12) | tile, ordered by
-// descending key-tile count (ties by position), so persistent CTAs start the longest items first.
+// Work items of p.tiles_per_item consecutive 128-row query tiles (1 for prefill_kernel, 2 for prefill_pair_kernel).
+// plan[0] = number of items of sequences with q_len >= min_q; plan[1 + i] = (seq << 12) | item of the sequence,
+// ordered by descending key-tile count of the item's last tile (ties by position), so persistent CTAs start the
+// longest items first.
 __global__ void __launch_bounds__(1024) prefill_plan_kernel(const PrefillParams p) {
   __shared__ int cost[kMaxPrefillTiles];
   __shared__ int code[kMaxPrefillTiles];
@@ -96,13 +95,14 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(const PrefillParams 
   // still read the plan) completes before the plan is rewritten; then the call's next kernel may start its blocks
   griddep_wait();
   if (tid == 0) griddep_launch_dependents();
-  // tiles per sequence and their exclusive prefix (B <= 1024: one element per thread)
+  // items per sequence and their exclusive prefix (B <= 1024: one element per thread)
+  const int tpi = p.tiles_per_item;
   int nt = 0, n = 0, L = 0;
   if (tid < p.num_seqs) {
     const int a = p.cu_q[tid];
     n = p.cu_q[tid + 1] - a;
     L = p.cu_k[tid + 1] - p.cu_k[tid];
-    nt = n >= p.min_q && n > 0 ? (n + 127) / 128 : 0;
+    nt = n >= p.min_q && n > 0 ? (n + 128 * tpi - 1) / (128 * tpi) : 0;
   }
   int x = nt;
 #pragma unroll
@@ -120,12 +120,11 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(const PrefillParams 
   const int off = before + x - nt;
   const int cap = min(p.q_tiles_bound, kMaxPrefillTiles);
   total = min(total, cap);
-  for (int qt = 0; qt < nt; ++qt) {
-    const int i = off + qt;
+  for (int u = 0; u < nt; ++u) {
+    const int i = off + u;
     if (i < cap) {
-      const int rows = min(128, n - qt * 128);
-      cost[i] = (L - n + qt * 128 + rows - 1) / 128 + 1;
-      code[i] = (tid << 12) | qt;
+      cost[i] = prefill_tile_nkv(n, L, min(tpi * u + tpi - 1, (n - 1) / 128));
+      code[i] = (tid << 12) | u;
     }
   }
   __syncthreads();
@@ -442,6 +441,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
               *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0u, 0u, 0u, 0u);
               *reinterpret_cast<uint4*>(vrow + kSlab + c * 16) = make_uint4(0u, 0u, 0u, 0u);
             }
+            // generic-proxy writes, read by the PV product through the async proxy: ordered by this fence and this
+            // thread's later PFULL arrival
+            fence_proxy_async_smem();
           }
         }
         alive = alive && mbar_wait_warp(&bars[B_SFULL + st], (g >> 1) & 1, abort);

@@ -51,6 +51,32 @@ def test_prefill_paged_prefix(cuda, q_lens, prefix):
     assert_attn_close(run_varlen(b), ref_varlen(b), f"paged prefix {q_lens}/{prefix}")
 
 
+# Calls with rows x heads >= 4 x SMs x 256 (4736 rows at 32 heads on 148 SMs) take the kernel with two query tiles
+# per work item (prefill_pair.cu); the cases above take the single-tile kernel.
+@pytest.mark.parametrize("lens", [[1024, 1000, 1300, 129, 1500]])
+def test_prefill_pair_contiguous(cuda, lens):
+    """Two-tile items: full pairs, a partial second tile (1000, 129 rows) and a lone last tile (1300, 1500 rows)."""
+    b = batch(lens, lens, seed=21, paged=False)
+    assert_attn_close(run_varlen(b, paged=False), ref_varlen(b, paged=False), f"pair contiguous {lens}")
+
+
+def test_prefill_pair_paged_prefix(cuda):
+    q_lens, prefix = [1024, 640, 1500, 1700], [0, 256, 1024, 300]
+    b = batch(q_lens, [q + p for q, p in zip(q_lens, prefix)], seed=22)
+    assert_attn_close(run_varlen(b), ref_varlen(b), "pair paged prefix")
+
+
+def test_prefill_pair_stale_nan_past_context(cuda):
+    q_lens, k_lens = [1300, 1200, 1100, 1200], [1400, 1333, 1900, 1250]
+    b = batch(q_lens, k_lens, seed=23)
+    ref = ref_varlen(b)
+    for i, L in enumerate(k_lens):
+        last = int(b.block_tables[i, (L + 255) // 256 - 1])
+        b.k_cache[last, L % 256 or 256:] = float("nan")
+        b.v_cache[last, L % 256 or 256:] = float("nan")
+    assert_attn_close(run_varlen(b), ref, "pair nan tail")
+
+
 def test_varlen_decode_rows_only(cuda):
     """A mixed step whose every run is short (decode rows with 1+k tokens): handled by the decode kernel."""
     q_lens = [1] * 20 + [5] * 10 + [12] * 3
