@@ -14,12 +14,13 @@
 //
 // Warp roles (384 threads): 0 = Q + K producer (also publishes the item descriptors), 3 = V producer, 1 = TMEM owner
 // + UMMA issuer, 2 idle, 4..7 and 8..11 = softmax + epilogue, one warpgroup per query tile: thread t of group w owns
-// query row t of tile w whole (128 exponentials per key tile, a quarter of them on the FMA pipe through exp2_poly2;
-// maximum and sum thread-local, so the groups never wait for each other), as two online-softmax steps of 64 keys
-// each: one TMEM load per half, and a P store that completes in the background while the second half loads.  The issuer interleaves the two tiles'
-// products, so one group's softmax runs while the tensor pipe works for the other.  Each group writes its
-// normalised O rows from registers to global memory and goes on to the next item, whose first S tiles the issuer
-// computes meanwhile.
+// query row t of tile w whole (128 exponentials per key tile on the MUFU pipe; maximum and sum thread-local, so the
+// groups never wait for each other), as two online-softmax steps of 64 keys each: one TMEM load per half, and a P
+// store that completes in the background while the second half loads.  A half first takes its weights against the
+// running maximum; only when a weight may have reached 2^8 (its half-row sum did) does it compute its own maximum
+// and redo them.  The issuer interleaves the two tiles' products, so one group's softmax runs while the tensor pipe
+// works for the other.  Each group writes its normalised O rows from registers to global memory and goes on to the
+// next item, whose first S tiles the issuer computes meanwhile.
 #include "nva_ptx.cuh"
 #include "nva_kernels.h"
 
@@ -375,69 +376,74 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 #pragma unroll
             for (int c = 0; c < 64; ++c) s[c] = c <= kmax ? s[c] : kNegInf;
           }
-          float m8[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            m8[i] = fmaxf(fmax3(fmax3(s[i], s[i + 8], s[i + 16]), s[i + 24], s[i + 32]),
-                          fmax3(s[i + 40], s[i + 48], s[i + 56]));
-          const float mx = fmaxf(fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), m8[6]), m8[7]);
-          const float m_cand = fmaxf(m_used, mx * p.scale_log2);
-          const bool rescale = m_used != kNegInf && m_cand > m_used + kRescaleLog2;
-          if (__any_sync(kFull, rescale)) {
-            const float alpha = rescale ? fast_exp2(m_used - m_cand) : 1.f;
-            if (j > 0) {
-              // the commit that reported S_w(j) also covers PV_w(j-1): O_w holds every earlier product of the item
-#pragma unroll 1
-              for (int c = 0; c < 128; c += 32) {
-                float ot[32];
-                tmem_ld32(t_lane + o_col + c, ot);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) ot[i] *= alpha;
-                tmem_st32(t_lane + o_col + c, ot);
-              }
-            }
-            if (h == 1) {   // the first half's P was taken against the old maximum
-              tmem_wait_st();
-              float pv[32];
-              tmem_ld32(t_lane + s_col, pv);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const uint32_t u = __float_as_uint(pv[i]);
-                pv[i] = __uint_as_float(pack_bf16x2(__uint_as_float(u << 16) * alpha,
-                                                    __uint_as_float(u & 0xffff0000u) * alpha));
-              }
-              tmem_st32(t_lane + s_col, pv);
-            }
-            if (rescale) l *= alpha;
-          }
-          if (rescale || m_used == kNegInf) m_used = m_cand;
-          // masked keys hold -inf, so their MUFU weights are exp2(-inf) = 0; a row that has seen no key yet
-          // (m_used = -inf) subtracts 0 and gets only zeros
-          const float neg_m = m_used == kNegInf ? 0.f : -m_used;
-          const float2 nm2 = make_float2(neg_m, neg_m);
-          float2 sum4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                            make_float2(0.f, 0.f)};
-          const bool full = kmax >= 63;
+          // Weights against the running maximum.  A half-row sum below 2^8 shows that no weight reached 2^8, i.e.
+          // this half did not raise the maximum past the rescale threshold: the half is done without computing its
+          // maximum.  Otherwise (or before the row's first key) the warp takes the exact path: maximum, rescale,
+          // weights again.  Masked keys hold -inf, so their weights are exp2(-inf) = 0; a row that has seen no key
+          // yet (m_used = -inf) subtracts 0 and gets only zeros.
           float pk[32];
+          float hsum = 0.f;
+          auto weights = [&]() {
+            const float neg_m = m_used == kNegInf ? 0.f : -m_used;
+            const float2 nm2 = make_float2(neg_m, neg_m);
+            float2 sum4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                              make_float2(0.f, 0.f)};
 #pragma unroll
-          for (int c = 0; c < 64; c += 2) {
-            const float2 x = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
-            float2 pp;
-            if ((c & 7) == 6) {   // a quarter of the exponentials on the FMA pipe (2^-126 at -inf: zero them)
-              pp = exp2_poly2(x);
-              if (!full) {
-                pp.x = c <= kmax ? pp.x : 0.f;
-                pp.y = c + 1 <= kmax ? pp.y : 0.f;
-              }
-            } else {
-              pp = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            for (int c = 0; c < 64; c += 2) {
+              const float2 x = ffma2(make_float2(s[c], s[c + 1]), sc2, nm2);
+              const float2 pp = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+              sum4[(c >> 1) & 3] = fadd2(sum4[(c >> 1) & 3], pp);
+              pk[c >> 1] = __uint_as_float(pack_bf16x2(pp.x, pp.y));
             }
-            sum4[(c >> 1) & 3] = fadd2(sum4[(c >> 1) & 3], pp);
-            pk[c >> 1] = __uint_as_float(pack_bf16x2(pp.x, pp.y));
+            const float2 s01 = fadd2(fadd2(sum4[0], sum4[1]), fadd2(sum4[2], sum4[3]));
+            hsum = s01.x + s01.y;
+          };
+          bool exact = m_used == kNegInf;
+          if (!__any_sync(kFull, exact)) {
+            weights();
+            exact = !(hsum < 256.f);
+          }
+          if (__any_sync(kFull, exact)) {
+            float m8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              m8[i] = fmaxf(fmax3(fmax3(s[i], s[i + 8], s[i + 16]), s[i + 24], s[i + 32]),
+                            fmax3(s[i + 40], s[i + 48], s[i + 56]));
+            const float mx = fmaxf(fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), m8[6]), m8[7]);
+            const float m_cand = fmaxf(m_used, mx * p.scale_log2);
+            const bool rescale = m_used != kNegInf && m_cand > m_used + kRescaleLog2;
+            if (__any_sync(kFull, rescale)) {
+              const float alpha = rescale ? fast_exp2(m_used - m_cand) : 1.f;
+              if (j > 0) {
+                // the commit that reported S_w(j) also covers PV_w(j-1): O_w holds every earlier product of the item
+#pragma unroll 1
+                for (int c = 0; c < 128; c += 32) {
+                  float ot[32];
+                  tmem_ld32(t_lane + o_col + c, ot);
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) ot[i] *= alpha;
+                  tmem_st32(t_lane + o_col + c, ot);
+                }
+              }
+              if (h == 1) {   // the first half's P was taken against the old maximum
+                tmem_wait_st();
+                float pv[32];
+                tmem_ld32(t_lane + s_col, pv);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  const uint32_t u = __float_as_uint(pv[i]);
+                  pv[i] = __uint_as_float(pack_bf16x2(__uint_as_float(u << 16) * alpha,
+                                                      __uint_as_float(u & 0xffff0000u) * alpha));
+                }
+                tmem_st32(t_lane + s_col, pv);
+              }
+              if (rescale) l *= alpha;
+            }
+            if (rescale || m_used == kNegInf) m_used = m_cand;
+            weights();
           }
           tmem_st32_nowait(t_lane + s_col + 32 * h, pk);
-          const float2 s01 = fadd2(fadd2(sum4[0], sum4[1]), fadd2(sum4[2], sum4[3]));
-          l += s01.x + s01.y;
+          l += hsum;
         }
         tmem_wait_st();
         tc_fence_before();
