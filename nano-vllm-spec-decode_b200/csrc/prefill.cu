@@ -7,8 +7,9 @@
 // list scheduling), so the long tiles start first and the short ones fill in wherever a CTA frees up.
 //
 // Per item: S = Q K^T with M = 128 query rows on the TMEM lanes, N = 128 keys (A = Q, B = K tile, both K-major
-// 128B-swizzled straight from TMA); P = exp2(S * scale - m) in bf16, written back into the first 64 columns of its
-// own S buffer in tensor memory; O += P V in TMEM (A = P read from TMEM, B = V tile, MN-major, straight from TMA).
+// 128B-swizzled straight from TMA); P = exp2(S * scale - m) in bf16, written back into its own S buffer in tensor
+// memory (keys [0, 64) in columns [0, 32), keys [64, 128) in columns [64, 96): each key half's P lands in that
+// half's own S columns); O += P V in TMEM (A = P read from TMEM, B = V tile, MN-major, straight from TMA).
 // Keeping P out of shared memory pays for a 3-stage V ring.  Each query row is shared by two threads, one per
 // key half (see the warp roles below).  O is rescaled in TMEM only when a row's maximum grows by more than 2^8
 // (until then P values up to 256 are exact enough in bf16 and FP32 sums).
@@ -16,8 +17,10 @@
 // Warp roles (384 threads): 0 = Q + K producer (also publishes the item descriptors), 3 = V producer, 1 = TMEM owner
 // + UMMA issuer, 2 = output writer, 4..11 = softmax + epilogue in two warpgroups: thread (group w, row t) owns keys
 // [64w, 64w + 64) of query row t, so each S tile costs a thread 64 exponentials (a quarter of them on the FMA pipe
-// through exp2_poly2) and two warps share each SM quarter to hide MUFU / TMEM latency.  The two halves of a row
-// exchange their maxima through shared memory and their sums through spare TMEM columns.  The softmax warps stage
+// through exp2_poly2) and two warps share each SM quarter to hide MUFU / TMEM latency.  A thread first takes its
+// weights against the row's running maximum; one named-barrier vote per tile tells whether any half-row sum reached
+// 2^8 (a weight may have), and only then do the two halves of each row exchange their maxima through shared memory
+// and redo the weights.  The row sums meet in spare TMEM columns.  The softmax warps stage
 // the normalised O tile in the item's Q buffer (TMA's 128-byte-swizzled two-slab layout) and move on; the writer
 // warp stores it (TMA for full 128-row tiles, plain stores for a sequence's last partial tile) and frees the buffer.
 #include "nva_ptx.cuh"
@@ -343,10 +346,11 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tc_fence_after();
       if (elect_one()) {
         const uint64_t vd = v_desc0 + ((st * kTile) >> 4);
-        const uint32_t pa = tmem + (gp & 1) * 128;   // P of tile gp: first 64 columns of its S buffer
+        const uint32_t pa = tmem + (gp & 1) * 128;   // P of tile gp: columns [0, 32) and [64, 96) of its S buffer
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)   // V: 16 keys (2048 B) per step; P: 8 columns per step; fresh O per item
-          umma_bf16_ts(tmem + 256, pa + kk * 8, vd + kk * (2048 >> 4), idesc_pv, (j_p > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + 256, pa + kk * 8 + (kk >= 4 ? 32 : 0), vd + kk * (2048 >> 4), idesc_pv,
+                       (j_p > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bars[B_ODONE]);
         umma_commit(&bars[B_VEMPTY + st]);
       }
@@ -448,57 +452,19 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         }
         alive = alive && mbar_wait_warp(&bars[B_SFULL + st], (g >> 1) & 1, abort);
         const int kmax = lim - j * 128 - c0;     // columns > kmax of this half are masked for this row
-        if (alive) {
-          tc_fence_after();
-          tmem_ld64(t_lane + st * 128 + c0, s);
-          if (kmax < 63) {
-#pragma unroll
-            for (int c = 0; c < 64; ++c) s[c] = c <= kmax ? s[c] : kNegInf;
-          }
-          float m8[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            m8[i] = fmaxf(fmax3(fmax3(s[i], s[i + 8], s[i + 16]), s[i + 24], s[i + 32]),
-                          fmax3(s[i + 40], s[i + 48], s[i + 56]));
-          mpart = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
-          red[(st * 2 + wg) * 128 + t] = mpart;
-        }
-        if (named_bar_any(1, 256, !alive)) {
-          alive = false;
-          break;
-        }
-        const float mx = fmaxf(mpart, red[(st * 2 + (wg ^ 1)) * 128 + t]);
-        const float m_cand = fmaxf(m_used, mx * p.scale_log2);
-        const bool rescale = m_used != kNegInf && m_cand > m_used + kRescaleLog2;
-        if (j > 0 && __any_sync(kFull, rescale)) {
-          // O must hold every earlier PV product of this item before it is rescaled
-          if (pv_seen < g) {
-            alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
-            pv_seen = g;
-          }
-          if (alive) {
-            const float alpha = rescale ? fast_exp2(m_used - m_cand) : 1.f;
-            tc_fence_after();
-#pragma unroll 1
-            for (int c = 0; c < 64; c += 32) {
-              float ot[32];
-              tmem_ld32(t_lane + 256 + c0 + c, ot);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) ot[i] *= alpha;
-              tmem_st32(t_lane + 256 + c0 + c, ot);
-            }
-            if (rescale) l *= alpha;
-          }
-        }
-        if (rescale || m_used == kNegInf) m_used = m_cand;
-        if (alive) {
-          // masked keys hold -inf, so their MUFU weights are exp2(-inf) = 0; a row that has seen no key yet
-          // (m_used = -inf) subtracts 0 and gets only zeros
+        // Weights against the running maximum (the same value in both halves of a row).  A half-row sum below 2^8
+        // shows that no weight reached 2^8, i.e. the row maximum did not grow past the rescale threshold on this
+        // half.  One vote per tile (the named barrier the maximum exchange used): when no thread needs more, the
+        // tile is done without its maximum; otherwise all take the exact path (maximum, exchange, rescale, weights
+        // again).  Masked keys hold -inf, so their MUFU weights are exp2(-inf) = 0; a row that has seen no key yet
+        // (m_used = -inf) subtracts 0 and gets only zeros.
+        float pk[32];
+        float hsum = 0.f;
+        auto weights = [&]() {
           const float neg_m = m_used == kNegInf ? 0.f : -m_used;
           const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(neg_m, neg_m);
           float2 sum4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                             make_float2(0.f, 0.f)};
-          float pk[32];
           const bool full = kmax >= 63;
 #pragma unroll
           for (int c = 0; c < 64; c += 2) {
@@ -516,10 +482,69 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
             sum4[(c >> 1) & 3] = fadd2(sum4[(c >> 1) & 3], pp);
             pk[c >> 1] = __uint_as_float(pack_bf16x2(pp.x, pp.y));
           }
-          // P (bf16 pairs, lower half = even key): keys [64 wg, 64 wg + 64) -> columns [32 wg, 32 wg + 32)
-          tmem_st32(t_lane + st * 128 + 32 * wg, pk);
           const float2 s01 = fadd2(fadd2(sum4[0], sum4[1]), fadd2(sum4[2], sum4[3]));
-          l += s01.x + s01.y;
+          hsum = s01.x + s01.y;
+        };
+        bool exact = true;
+        if (alive) {
+          tc_fence_after();
+          tmem_ld64(t_lane + st * 128 + c0, s);
+          if (kmax < 63) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) s[c] = c <= kmax ? s[c] : kNegInf;
+          }
+          if (m_used != kNegInf) {
+            weights();
+            exact = !(hsum < 256.f);
+            tmem_st32_nowait(t_lane + st * 128 + 64 * wg, pk);
+          }
+        }
+        if (named_bar_any(1, 256, !alive || exact)) {
+          if (named_bar_any(1, 256, !alive)) {
+            alive = false;
+            break;
+          }
+          float m8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            m8[i] = fmaxf(fmax3(fmax3(s[i], s[i + 8], s[i + 16]), s[i + 24], s[i + 32]),
+                          fmax3(s[i + 40], s[i + 48], s[i + 56]));
+          mpart = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+          red[(st * 2 + wg) * 128 + t] = mpart;
+          named_bar_sync(1, 256);
+          const float mx = fmaxf(mpart, red[(st * 2 + (wg ^ 1)) * 128 + t]);
+          const float m_cand = fmaxf(m_used, mx * p.scale_log2);
+          const bool rescale = m_used != kNegInf && m_cand > m_used + kRescaleLog2;
+          if (j > 0 && __any_sync(kFull, rescale)) {
+            // O must hold every earlier PV product of this item before it is rescaled
+            if (pv_seen < g) {
+              alive = mbar_wait_warp(&bars[B_ODONE], (g - 1) & 1, abort);
+              pv_seen = g;
+            }
+            if (alive) {
+              const float alpha = rescale ? fast_exp2(m_used - m_cand) : 1.f;
+              tc_fence_after();
+#pragma unroll 1
+              for (int c = 0; c < 64; c += 32) {
+                float ot[32];
+                tmem_ld32(t_lane + 256 + c0 + c, ot);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) ot[i] *= alpha;
+                tmem_st32(t_lane + 256 + c0 + c, ot);
+              }
+              if (rescale) l *= alpha;
+            }
+          }
+          if (rescale || m_used == kNegInf) m_used = m_cand;
+          weights();
+          tmem_wait_st();   // the fast path's store of these columns (if any) lands first
+          tmem_st32_nowait(t_lane + st * 128 + 64 * wg, pk);
+        }
+        if (alive) {
+          // P (bf16 pairs, lower half = even key): keys [64 wg, 64 wg + 64) -> columns [64 wg, 64 wg + 32), the
+          // group's own S columns (already in registers), so it may be written before the other group has read its half
+          tmem_wait_st();
+          l += hsum;
           // Observe PV(g-1) before handing over P(g), so that at most one PV product is ever unobserved: otherwise
           // P(g+1) could complete the PFULL phase after P(g) before the issuer saw P(g)'s (its parity wait would
           // then wait for a phase that needs PV(g) itself), and PV(g) could complete ODONE before this wait for
