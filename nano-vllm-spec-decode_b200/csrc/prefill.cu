@@ -496,6 +496,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           if (m_used != kNegInf) {
             weights();
             exact = !(hsum < 256.f);
+            // P (bf16 pairs, lower half = even key): keys [64 wg, 64 wg + 64) -> columns [64 wg, 64 wg + 32), this
+            // group's own S columns (already in registers), so it may land before the other group has read its half
             tmem_st32_nowait(t_lane + st * 128 + 64 * wg, pk);
           }
         }
@@ -541,9 +543,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           tmem_st32_nowait(t_lane + st * 128 + 64 * wg, pk);
         }
         if (alive) {
-          // P (bf16 pairs, lower half = even key): keys [64 wg, 64 wg + 64) -> columns [64 wg, 64 wg + 32), the
-          // group's own S columns (already in registers), so it may be written before the other group has read its half
-          tmem_wait_st();
+          tmem_wait_st();   // this group's P stores (above) complete
           l += hsum;
           // Observe PV(g-1) before handing over P(g), so that at most one PV product is ever unobserved: otherwise
           // P(g+1) could complete the PFULL phase after P(g) before the issuer saw P(g)'s (its parity wait would
