@@ -77,6 +77,21 @@ def test_prefill_pair_stale_nan_past_context(cuda):
     assert_attn_close(run_varlen(b), ref, "pair nan tail")
 
 
+@pytest.mark.parametrize("lens", [[700, 300], [1200, 1200, 1200, 1200]])
+def test_prefill_rising_scores_rescale_every_half_tile(cuda, lens):
+    """Scores that rise along the keys: dim 0 of every query is 4 and dim 0 of key p gains 0.3 p, so each 64 keys
+    raise a row's log2 score by ~9.8, past the 2^8 rescale threshold.  Every key tile then rescales O, and every
+    second 64-key half rescales the first half's P (the two-tile kernel) or takes the exact vote path (the single-tile
+    kernel).  [700, 300] runs the single-tile kernel, 4 x 1200 rows the two-tile one."""
+    b = batch(lens, lens, seed=31, paged=False)
+    cu = b.cu_seqlens_k.tolist()
+    for i in range(len(lens)):
+        pos = torch.arange(lens[i], device=cuda, dtype=torch.float32)
+        b.k_new[cu[i]:cu[i + 1], :, 0] += (0.3 * pos)[:, None].to(b.k_new.dtype)
+    b.q[:, :, 0] = 4.0
+    assert_attn_close(run_varlen(b, paged=False), ref_varlen(b, paged=False), f"rising scores {lens}")
+
+
 def test_varlen_decode_rows_only(cuda):
     """A mixed step whose every run is short (decode rows with 1+k tokens): handled by the decode kernel."""
     q_lens = [1] * 20 + [5] * 10 + [12] * 3
