@@ -80,6 +80,21 @@ def test_verify_config3_full(cuda, k):
     assert_attn_close(run_decode(b), ref_decode(b), f"config3 k={k}")
 
 
+@pytest.mark.parametrize("n", [1, 5])
+def test_rising_scores_rescale_and_merge(cuda, n):
+    """Scores that rise along the keys (dim 0 of every query is 4, dim 0 of key p gains 0.3 p: ~9.8 in log2 units
+    per 64 keys): every tile moves the row maxima past the 2^8 rescale threshold, and the pieces of a split sequence
+    reach the in-kernel merge with log-sum-exps hundreds of log2 units apart."""
+    lens = [2000, 700, 129, 4000]
+    b = batch(lens, n=n, seed=41)
+    for i, L in enumerate(lens):
+        pos = torch.arange(L, device=cuda)
+        pages = b.block_tables[i, pos // 256].long()
+        b.k_cache[pages, pos % 256, :, 0] += (0.3 * pos.float())[:, None].to(b.k_cache.dtype)
+    b.q[:, :, 0] = 4.0
+    assert_attn_close(run_decode(b), ref_decode(b), f"rising scores n={n}")
+
+
 def test_padding_sequences_zero_and_invariant(cuda):
     """Padded sequences (length 0, table -1) output zeros, and real rows are bitwise identical with and without
     the padding (the check_padding.py property that eager == CUDA-graph runs rely on)."""
