@@ -133,8 +133,6 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   if (p.wait_primary) griddep_wait();
   if (tid == 0) griddep_launch_dependents();
   const int total = p.plan[0];
-  // Register split: the launch gives 384 x 168; the service warpgroup (warps 0-3) keeps 56 a thread and the two
-  // softmax warpgroups take 224 (128 x 56 + 256 x 224 = 384 x 168), room for a whole row of S.
 
   if (warp == 0 || warp == 3) {
     // ------------------------------------------------------------ Q+K (warp 0) and V (warp 3) producers
