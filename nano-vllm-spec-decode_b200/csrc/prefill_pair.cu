@@ -42,8 +42,8 @@ constexpr int kVStages = 3;
 constexpr int kOffQ = 0;                              // Q tile of group 0, Q tile of group 1
 constexpr int kOffK = kOffQ + 2 * kTile;              // K ring
 constexpr int kOffV = kOffK + kKStages * kTile;       // V ring
-constexpr int kOffBars = kOffV + kVStages * kTile;    // 32 x u64
-constexpr int kOffItems = kOffBars + 32 * 8;          // kItemRing x 2 x int4
+constexpr int kOffBars = kOffV + kVStages * kTile;    // 40 x u64
+constexpr int kOffItems = kOffBars + 40 * 8;          // kItemRing x 2 x int4
 constexpr int kOffTmem = kOffItems + kItemRing * 32;
 constexpr int kOffAbort = kOffTmem + 4;
 constexpr int kSmemBytes = kOffAbort + 4;             // the dynamic shared memory base is 1024-aligned (checked)
@@ -52,8 +52,11 @@ static_assert(kSmemBytes <= 232448, "prefill shared memory budget");
 // barriers; "w" entries come in pairs, one per query tile of the item (softmax group w)
 enum {
   B_QFULL = 0, B_QEMPTY = 2, B_KFULL = 4, B_KEMPTY = 6, B_VFULL = 8, B_VEMPTY = 11, B_SFULL = 14, B_PFULL = 16,
-  B_ODONE = 18, B_ITEM = 20   // B_ITEM + kItemRing <= 32
+  B_ODONE = 18, B_ITEM = 20,
+  B_IREAD = 28   // kItemRing: every consuming warp has read the entry (B_IREAD + kItemRing <= 40)
 };
+// warps that read each item descriptor: the V producer, the issuer and the eight softmax warps
+constexpr int kItemReaders = 10;
 
 struct Item {
   int b, qp, h;        // sequence, query tile pair (tiles 2 qp and 2 qp + 1), q head
@@ -112,7 +115,10 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_init(&bars[B_VFULL + i], 1);
       mbar_init(&bars[B_VEMPTY + i], 1);
     }
-    for (int i = 0; i < kItemRing; ++i) mbar_init(&bars[B_ITEM + i], 1);
+    for (int i = 0; i < kItemRing; ++i) {
+      mbar_init(&bars[B_ITEM + i], 1);
+      mbar_init(&bars[B_IREAD + i], kItemReaders);
+    }
     *abort = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -146,12 +152,16 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     bool stop = false;
     int* counter = p.plan + 1 + p.q_tiles_bound;
     // The K producer takes each item and publishes it (nkv = 0: no more items) in the item ring; the V producer,
-    // the UMMA issuer and the softmax warps follow the ring.  The ring cannot overrun: the K producer waits for each
-    // Q buffer's previous tile, whose last S product follows the softmax warps' P of the item before.
+    // the UMMA issuer and the softmax warps follow the ring, and each of those warps reports on B_IREAD that it has
+    // read an entry, which the producer waits for before it writes the entry again (softmax group 1 skips the items
+    // without a second tile, so no other wait bounds how far it may lag).
     for (int it_count = 0; !stop; ++it_count) {
       const int e = it_count % kItemRing;
       Item it;
       if (is_k) {
+        if (it_count >= kItemRing &&
+            !mbar_wait_warp(&bars[B_IREAD + e], ((it_count / kItemRing) + 1) & 1, abort))
+          break;
         int k = blockIdx.x;
         if (it_count > 0) {
           int v = 0;
@@ -169,6 +179,8 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       } else {
         if (!mbar_wait_warp(&bars[B_ITEM + e], (it_count / kItemRing) & 1, abort)) break;
         const int4 i0 = items[2 * e];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[B_IREAD + e]);
         if (i0.w == 0) break;
         it.b = i0.x;
         it.h = i0.z;
@@ -247,6 +259,8 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       const int e = it_count % kItemRing;
       if (!mbar_wait_warp(&bars[B_ITEM + e], (it_count / kItemRing) & 1, abort)) break;
       const int4 i0 = items[2 * e], i1 = items[2 * e + 1];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[B_IREAD + e]);
       const int nkv = i0.w;
       if (nkv == 0) break;
       const int n0 = i1.w >> 16, n1 = i1.w & 0xffff;
@@ -327,6 +341,8 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       const int e = it_count % kItemRing;
       if (!mbar_wait_warp(&bars[B_ITEM + e], (it_count / kItemRing) & 1, abort)) break;
       const int4 i0 = items[2 * e], i1 = items[2 * e + 1];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[B_IREAD + e]);
       const int nkv = i0.w;
       if (nkv == 0) break;
       const int n0 = i1.w >> 16, n1 = i1.w & 0xffff;
