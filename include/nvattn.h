@@ -121,6 +121,30 @@ NVA_API int nva_greedy_accept(const void* target_ids, int64_t target_row_stride,
                               int32_t id_bytes, void* num_accepted, void* next_tokens, void* stream);
 
 /*
+ * Greedy verify from vocabulary shards.  Replaces, for all-greedy verify steps, the logits gather to rank 0 in
+ * ParallelLMHead.forward (nanovllm/layers/embed_head.py:56-68) and the argmax + accept rule of verify_drafts
+ * (nanovllm/layers/sampler.py:66-82).
+ *
+ * nva_shard_argmax: one rank's logits shard [rows, vocab_shard] (bf16 when elem_bytes == 2, float when 4, row
+ * stride in elements) -> keys[rows], one uint64 per row:
+ *     keys[r] = orderable(max_j logits[r, j]) << 32 | (0xFFFFFFFF - (vocab_offset + first j of that maximum))
+ * where orderable() maps floats to unsigned integers in order (NaN above +inf, -0 equal to +0).  The largest key
+ * over all shards names the argmax of the concatenated row with torch's tie rule (lowest index).  keys are
+ * cleared in stream order by the call (one memset node, then the kernel).  rows <= 65535,
+ * vocab_offset + vocab_shard < 2^32.
+ *
+ * nva_shard_accept: keys [num_shards, num_seqs * (k+1)] (shard-major, e.g. gathered from every rank) -> the target
+ * ids (the merged argmaxes) and the greedy accept rule of nva_greedy_accept on them: num_accepted[s] = unbroken run
+ * of target[s, j] == draft[s, j] with j < num_drafts[s], next_token[s] = target[s, num_accepted[s]].  Ids are
+ * int32 (id_bytes 4) or int64 (8).  k == 0 gives plain greedy sampling (next_token = argmax of the row).
+ */
+NVA_API int nva_shard_argmax(const void* logits, int64_t row_stride, int32_t rows, int32_t vocab_shard,
+                             int64_t vocab_offset, int32_t elem_bytes, uint64_t* keys, void* stream);
+NVA_API int nva_shard_accept(const uint64_t* keys, int32_t num_shards, int32_t num_seqs, int32_t k,
+                             const void* draft_ids, int64_t draft_row_stride, const void* num_drafts, int32_t id_bytes,
+                             void* num_accepted, void* next_tokens, void* stream);
+
+/*
  * Paged decode / verify attention without a caller workspace.  No counterpart in the reference: nano-vllm always
  * lets flash-attn allocate.  Same arguments and results as nva_paged_decode, minus the workspace.
  * It serves callers that cannot allocate device memory -- code running inside an allocator hook or a host callback
@@ -133,8 +157,10 @@ NVA_API int nva_greedy_accept(const void* target_ids, int64_t target_row_stride,
  *  - A call needing more than NVA_NOALLOC_SCRATCH_BYTES (2 x SMs x rows x 129 x 4 bytes, rows = q_per_seq x
  *    num_heads / num_kv_heads rounded up to 16, 32 or 48) returns NVA_ERR_WORKSPACE before launching anything; on a
  *    148-SM B200 that admits up to 32 rows (decode, and verify with up to 7 drafts at 4 q heads per kv head).
- *  - All calls on a device share the array and leave their contents in it; nothing in it needs clearing between
- *    calls, but calls that overlap on the GPU (e.g. on two streams) race on it and must be serialised by the caller.
+ *  - All calls on a device share the array and leave their contents in it.  The caller never clears it: each call
+ *    first issues a small memset of the array's merge tickets on `stream`, then the kernel (two operations in stream
+ *    order).  Calls that overlap on the GPU (e.g. on two streams) race on the array and must be serialised by the
+ *    caller.
  */
 #define NVA_NOALLOC_SCRATCH_BYTES (6u << 20)
 NVA_API int nva_paged_decode_noalloc(const void* q, int64_t q_row_stride, const void* k_cache, const void* v_cache,

@@ -15,12 +15,10 @@
 namespace nva {
 // The device error word (bits in include/nvattn.h); defined here so the host accessors below own its symbol.
 __device__ uint32_t g_error_word = 0;
-}  // namespace nva
-
-namespace {
 
 thread_local char g_last_cuda_error[256] = "";
 
+// Host helpers shared with paged_decode_noalloc.cu (declared in nva_kernels.h).
 int cuda_fail(cudaError_t e) {
   snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
   return NVA_ERR_CUDA;
@@ -39,19 +37,6 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-int sm_count() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  static int cached[64] = {0};
-  if (dev < 64 && cached[dev] > 0) return cached[dev];
-  int n = 0;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-  if (dev < 64) cached[dev] = n;
-  return n;
-}
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
 // Rank-3 bf16 view {128 dims, heads, rows} with the given row stride (bytes), 64 x 1 x 128 boxes, 128B swizzle.
 int encode_rows(CUtensorMap* tm, const void* base, int64_t heads, int64_t rows, int64_t row_stride_bytes) {
   auto fn = encode_fn();
@@ -69,6 +54,27 @@ int encode_rows(CUtensorMap* tm, const void* base, int64_t heads, int64_t rows, 
   }
   return NVA_OK;
 }
+
+}  // namespace nva
+
+namespace {
+
+using nva::cuda_fail;
+using nva::encode_rows;
+using nva::g_last_cuda_error;
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  static int cached[64] = {0};
+  if (dev < 64 && cached[dev] > 0) return cached[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int check_cache(const void* k_cache, const void* v_cache, int32_t num_blocks, int32_t block_size, int32_t kvh) {
   if (k_cache == nullptr || v_cache == nullptr || num_blocks <= 0 || block_size <= 0 || kvh <= 0)
@@ -261,8 +267,10 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
   CUtensorMap tm_q, tm_o;
   bool o_tma = false;
   // Work items of two query tiles (prefill_pair_kernel) share each K / V tile between two softmax groups, faster per
-  // tile, but halve the number of items: chosen when the call's rows x heads give at least four such items per SM.
-  const bool pair = static_cast<int64_t>(total_q) * num_heads >= 4LL * grid * 256;
+  // tile, but halve the number of items: chosen when the call's rows x heads give at least four such items per SM
+  // and some query run can fill two tiles (max_seqlen_q > 128: with shorter runs every item would have one tile and
+  // half of the pair kernel's softmax warps would idle).
+  const bool pair = max_seqlen_q > 128 && static_cast<int64_t>(total_q) * num_heads >= 4LL * grid * 256;
   if (long_runs) {
     if ((rc = encode_rows(&tm_q, q, num_heads, total_q, q_row_stride * 2)) != NVA_OK) return rc;
     // single-tile kernel: full 128-row output tiles leave through TMA stores when the output rows allow a tensor map
@@ -338,6 +346,35 @@ NVA_API int nva_greedy_accept(const void* target_ids, int64_t target_row_stride,
   cudaError_t e = nva::launch_greedy_accept(target_ids, target_row_stride, draft_ids, draft_row_stride, num_drafts,
                                             num_seqs, k, id_bytes, num_accepted, next_tokens,
                                             static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? NVA_OK : cuda_fail(e);
+}
+
+NVA_API int nva_shard_argmax(const void* logits, int64_t row_stride, int32_t rows, int32_t vocab_shard,
+                             int64_t vocab_offset, int32_t elem_bytes, uint64_t* keys, void* stream) {
+  if (rows < 0 || vocab_shard < 0 || vocab_offset < 0) return NVA_ERR_INVALID_ARGUMENT;
+  if (elem_bytes != 2 && elem_bytes != 4) return NVA_ERR_UNSUPPORTED;
+  if (rows == 0) return NVA_OK;
+  if (logits == nullptr || keys == nullptr || vocab_shard == 0 || row_stride < vocab_shard)
+    return NVA_ERR_INVALID_ARGUMENT;
+  if (rows > 65535 || vocab_offset + vocab_shard > int64_t(0xFFFFFFFF)) return NVA_ERR_UNSUPPORTED;
+  const int sms = sm_count();
+  if (sms <= 0) return cuda_fail(cudaGetLastError());
+  cudaError_t e = nva::launch_shard_argmax(logits, row_stride, rows, vocab_shard, static_cast<uint32_t>(vocab_offset),
+                                           elem_bytes, keys, sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? NVA_OK : cuda_fail(e);
+}
+
+NVA_API int nva_shard_accept(const uint64_t* keys, int32_t num_shards, int32_t num_seqs, int32_t k,
+                             const void* draft_ids, int64_t draft_row_stride, const void* num_drafts, int32_t id_bytes,
+                             void* num_accepted, void* next_tokens, void* stream) {
+  if (num_seqs < 0 || k < 0 || num_shards <= 0) return NVA_ERR_INVALID_ARGUMENT;
+  if (id_bytes != 4 && id_bytes != 8) return NVA_ERR_UNSUPPORTED;
+  if (num_seqs == 0) return NVA_OK;
+  if (keys == nullptr || num_drafts == nullptr || num_accepted == nullptr || next_tokens == nullptr)
+    return NVA_ERR_INVALID_ARGUMENT;
+  if (k > 0 && (draft_ids == nullptr || draft_row_stride < k)) return NVA_ERR_INVALID_ARGUMENT;
+  cudaError_t e = nva::launch_shard_accept(keys, num_shards, num_seqs, k, draft_ids, draft_row_stride, num_drafts,
+                                           id_bytes, num_accepted, next_tokens, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? NVA_OK : cuda_fail(e);
 }
 

@@ -128,4 +128,18 @@ cudaError_t launch_greedy_accept(const void* target, int64_t target_row_stride, 
                                  int64_t draft_row_stride, const void* num_drafts, int32_t num_seqs, int32_t k,
                                  int32_t id_bytes, void* num_accepted, void* next_tokens, cudaStream_t stream);
 
+// Host helpers of the C ABI (capi.cu): record a CUDA error's text for nva_last_cuda_error() and return NVA_ERR_CUDA;
+// encode a rank-3 bf16 tensor map {128 dims, heads, rows} (row stride in bytes) with 64 x 1 x 128 boxes and 128-byte
+// swizzle, the layout every TMA load of the kernels uses (an encoder failure is recorded the same way).
+int cuda_fail(cudaError_t e);
+int encode_rows(CUtensorMap* tm, const void* base, int64_t heads, int64_t rows, int64_t row_stride_bytes);
+
+// Per-row (max, index) keys of a vocabulary shard of logits (bf16 when elem_bytes == 2, float when 4), and the merge
+// of several shards' keys into greedy accept lengths; see shard_argmax.cu.
+cudaError_t launch_shard_argmax(const void* logits, int64_t row_stride, int32_t rows, int32_t vocab,
+                                uint32_t vocab_offset, int32_t elem_bytes, void* keys, int sms, cudaStream_t stream);
+cudaError_t launch_shard_accept(const void* keys, int32_t num_shards, int32_t num_seqs, int32_t k, const void* drafts,
+                                int64_t draft_row_stride, const void* num_drafts, int32_t id_bytes,
+                                void* num_accepted, void* next_tokens, cudaStream_t stream);
+
 }  // namespace nva

@@ -469,7 +469,9 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // 2^x on the FMA/ALU pipes (no MUFU): Cody-Waite split x = n + f with n = rint(x), f in [-0.5, 0.5]; 2^f from a
 // degree-3 polynomial fitted here by iteratively reweighted least squares to minimise the relative error on that
 // interval (max relative error 7.5e-5, far below bf16's 2^-8); 2^n added into the exponent field.  x is clamped to
-// [-126, 126]; callers use it for softmax weights exp2(s - m) <= 2^8.
+// [-126, 126]; callers use it for softmax weights exp2(s - m) <= 2^8.  At the bottom (n = -126 with 2^f's polynomial
+// below 1: x within ~1e-4 above -126, and clamped inputs) the result is a subnormal with relative error up to 1.5e-4
+// (absolute error below 2^-138), which no softmax row sum (>= 1) can see.
 __device__ __forceinline__ float exp2_poly(float x) {
   x = fminf(fmaxf(x, -126.0f), 126.0f);
   const float magic = 12582912.0f;   // 1.5 * 2^23: adding it rounds x to an integer held in the low mantissa bits

@@ -17,7 +17,6 @@
 //    say) race on the array and must be serialised by the caller;
 //  - a call that needs more than NVA_NOALLOC_SCRATCH_BYTES is rejected with NVA_ERR_WORKSPACE before any launch;
 //  - nothing here allocates: no cudaMalloc, no cudaFree, no allocating library routine.
-#include <cudaTypedefs.h>
 #include <mutex>
 
 #include "../../include/nvattn.h"
@@ -37,47 +36,23 @@ int g_sm_count[kMaxDevices] = {};
 // Device address of the scratch and the SM count of the current device, looked up once per device.
 int current_device_scratch(void** addr, int* sms) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return NVA_ERR_CUDA;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return nva::cuda_fail(e);
   if (dev < 0 || dev >= kMaxDevices) return NVA_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (g_scratch_addr[dev] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return NVA_ERR_CUDA;
+    if ((e = cudaGetSymbolAddress(&p, g_noalloc_scratch)) != cudaSuccess) return nva::cuda_fail(e);
+    if (p == nullptr) return nva::cuda_fail(cudaErrorInvalidSymbol);
     int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
-      return NVA_ERR_CUDA;
+    if ((e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return nva::cuda_fail(e);
+    if (n <= 0) return nva::cuda_fail(cudaErrorInvalidDevice);
     g_sm_count[dev] = n;
     g_scratch_addr[dev] = p;
   }
   *addr = g_scratch_addr[dev];
   *sms = g_sm_count[dev];
   return NVA_OK;
-}
-
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// {128 dims, heads, rows} bf16 view of a KV cache, 64 x 1 x 128 boxes with 128-byte swizzle (the kernels' layout).
-bool cache_map(CUtensorMap* tm, const void* base, int64_t heads, int64_t rows) {
-  auto fn = tensor_map_encoder();
-  if (fn == nullptr) return false;
-  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[2] = {128 * 2, static_cast<cuuint64_t>(heads * 128 * 2)};
-  cuuint32_t box[3] = {64, 1, 128};
-  cuuint32_t estr[3] = {1, 1, 1};
-  return fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -121,8 +96,9 @@ extern "C" NVA_API int nva_paged_decode_noalloc(const void* q, int64_t q_row_str
 
   CUtensorMap tm_k, tm_v;
   const int64_t rows = static_cast<int64_t>(num_blocks) * block_size;
-  if (!cache_map(&tm_k, k_cache, num_kv_heads, rows) || !cache_map(&tm_v, v_cache, num_kv_heads, rows))
-    return NVA_ERR_CUDA;
+  const int64_t row_bytes = static_cast<int64_t>(num_kv_heads) * head_dim * 2;
+  if ((rc = nva::encode_rows(&tm_k, k_cache, num_kv_heads, rows, row_bytes)) != NVA_OK) return rc;
+  if ((rc = nva::encode_rows(&tm_v, v_cache, num_kv_heads, rows, row_bytes)) != NVA_OK) return rc;
 
   nva::DecodeParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -153,5 +129,5 @@ extern "C" NVA_API int nva_paged_decode_noalloc(const void* q, int64_t q_row_str
   // (a plain launch: the operation before the kernel is the memset, not a kernel)
   if (e == cudaSuccess)
     e = nva::launch_paged_decode(tm_k, tm_v, p, np, grid, static_cast<cudaStream_t>(stream), false);
-  return e == cudaSuccess ? NVA_OK : NVA_ERR_CUDA;
+  return e == cudaSuccess ? NVA_OK : nva::cuda_fail(e);
 }

@@ -37,15 +37,42 @@ def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     call leaves them zero, so it is allocated zero-filled once (grown, zero-filled, when a call needs more) and then
     reused by every call and every captured graph.  Calls on one device are ordered by the stream they run on:
     nano-vllm runs attention from one stream; concurrent streams on one device need their own workspaces through
-    the C ABI."""
+    the C ABI.  Growing it while a CUDA graph is being captured would allocate from the graph's pool and record the
+    zero-fill into every replay, so that raises instead: size it first with reserve_workspace (the nano-vllm drop-in
+    does so when the KV cache is allocated)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     ws = _WORKSPACES.get(idx)
     if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(f"nvattn: the attention workspace of cuda:{idx} must grow to {nbytes} bytes during a "
+                               "CUDA graph capture; call nvattn.ops.reserve_workspace(...) before capturing")
         if ws is not None:
             _RETIRED.append(ws)
         ws = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=device)
         _WORKSPACES[idx] = ws
     return ws
+
+
+def reserve_workspace(max_num_seqs: int, max_num_tokens: int, num_heads: int, num_kv_heads: int,
+                      head_dim: int = 128, device: torch.device | None = None) -> int:
+    """Allocate (zero-filled) the workspace every later decode / verify / varlen call of up to max_num_seqs
+    sequences and max_num_tokens query rows needs on `device`, so that no call, captured or not, allocates.
+    Returns its size in bytes.  nano-vllm: max_num_seqs and max_num_batched_tokens of its Config."""
+    device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        need = max(lib.nva_varlen_workspace_bytes(max_num_seqs, max_num_tokens, num_heads, num_kv_heads, head_dim),
+                   max(lib.nva_paged_decode_workspace_bytes(max_num_seqs, n, num_heads, num_kv_heads, head_dim)
+                       for n in range(1, 49)))
+    return _workspace(need, device).numel()
+
+
+def reset_workspaces() -> None:
+    """Zero-fill every workspace again.  A call that gave up on a pipeline wait (bit 2 of the device error word) may
+    leave merge tickets non-zero, after which later calls could merge split pieces wrongly; call this (outside any
+    graph capture, after clearing the error word) before going on."""
+    for ws in list(_WORKSPACES.values()) + _RETIRED:
+        ws.zero_()
 
 
 def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -158,4 +185,39 @@ def greedy_accept(target_ids: torch.Tensor, draft_ids: torch.Tensor, num_drafts:
         target_ids.data_ptr(), target_ids.stride(0), draft_ids.data_ptr() if K else 0, draft_ids.stride(0) if K else 0,
         num_drafts.data_ptr(), S, K, target_ids.element_size(), acc.data_ptr(), nxt.data_ptr(), _stream()),
         "greedy accept")
+    return acc, nxt
+
+
+def shard_argmax(logits: torch.Tensor, vocab_offset: int = 0) -> torch.Tensor:
+    """Per-row argmax keys of one vocabulary shard of logits [rows, V_shard] (bf16 or float32, unit column stride):
+    int64 [rows] holding orderable(max) << 32 | (0xFFFFFFFF - (vocab_offset + first index of the max)) as raw bits.
+    The largest key of a row over all shards (compared as unsigned) is the row's argmax with torch's tie rule; see
+    shard_accept.  Replaces the per-rank part of the logits gather + argmax (embed_head.py:56-68, sampler.py:66)."""
+    _need_cuda(logits)
+    assert logits.dim() == 2 and logits.stride(-1) == 1
+    assert logits.dtype in (torch.bfloat16, torch.float32)
+    rows, vocab = logits.shape
+    keys = torch.empty(rows, dtype=torch.int64, device=logits.device)
+    _lib.check(_lib.load().nva_shard_argmax(logits.data_ptr(), logits.stride(0), rows, vocab, int(vocab_offset),
+                                            logits.element_size(), keys.data_ptr(), _stream()), "shard argmax")
+    return keys
+
+
+def shard_accept(keys: torch.Tensor, draft_ids: torch.Tensor, num_drafts: torch.Tensor):
+    """Greedy accept from argmax keys: keys [num_shards, S, K+1] (int64 raw bits from shard_argmax of each shard,
+    contiguous), draft_ids [S, K], num_drafts [S] (int32 or int64, same dtype).  Returns (num_accepted [S],
+    next_token [S]) in that dtype: verify_drafts' greedy result (sampler.py:66-82) on the concatenated shards."""
+    _need_cuda(keys, draft_ids, num_drafts)
+    num_shards, S, K1 = keys.shape
+    K = K1 - 1
+    dt = draft_ids.dtype
+    assert keys.dtype == torch.int64 and keys.is_contiguous()
+    assert dt in (torch.int32, torch.int64) and num_drafts.dtype == dt
+    assert num_drafts.is_contiguous() and num_drafts.numel() == S
+    assert draft_ids.shape == (S, K) and (K == 0 or draft_ids.stride(-1) == 1)
+    acc = torch.empty(S, dtype=dt, device=keys.device)
+    nxt = torch.empty(S, dtype=dt, device=keys.device)
+    _lib.check(_lib.load().nva_shard_accept(
+        keys.data_ptr(), num_shards, S, K, draft_ids.data_ptr() if K else 0, draft_ids.stride(0) if K else 0,
+        num_drafts.data_ptr(), draft_ids.element_size(), acc.data_ptr(), nxt.data_ptr(), _stream()), "shard accept")
     return acc, nxt

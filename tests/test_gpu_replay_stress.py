@@ -1,5 +1,6 @@
 """Long CUDA-graph replay runs of the full-size decode (config 2), verify (config 3, k = 8) and mixed (config 4)
-steps and of a prefill of sixteen 1024-token prompts, as nano-vllm replays its captured steps: every replay must finish without any bounded wait giving up (the
+steps, of a prefill of sixteen 1024-token prompts and of the two-tile prefill kernel on sixty-four prompts of at most
+128 tokens (every item one tile), as nano-vllm replays its captured steps: every replay must finish without any bounded wait giving up (the
 device error word stays 0) and give bitwise the same output as the eager call (the kernels are deterministic:
 the split, the merge order and each item's arithmetic depend only on the inputs).  Timing-dependent races between
 the kernels' warp roles, or between the chained kernels of a varlen call, would show up here as a set error bit or
@@ -48,13 +49,20 @@ def _varlen_call(b, out):
     return call
 
 
-@pytest.mark.parametrize("case", ["decode_config2", "verify_config3_k8", "mixed_config4", "prefill_16x1024"])
+@pytest.mark.parametrize("case", ["decode_config2", "verify_config3_k8", "mixed_config4", "prefill_16x1024",
+                                  "prefill_pair_short_items"])
 def test_graph_replays_stay_clean_and_bitwise_stable(cuda, case):
     from nvattn import _lib
     from nvattn.workloads import decode_config, mixed_config, varlen_batch, verify_config
-    if case in ("mixed_config4", "prefill_16x1024"):
-        b = (mixed_config(seed=0, device="cuda") if case == "mixed_config4"
-             else varlen_batch([1024] * 16, [1024] * 16, 32, 8, 128, 64, 0.5, 42, device="cuda", paged=False))
+    if case in ("mixed_config4", "prefill_16x1024", "prefill_pair_short_items"):
+        if case == "mixed_config4":
+            b = mixed_config(seed=0, device="cuda")
+        elif case == "prefill_16x1024":
+            b = varlen_batch([1024] * 16, [1024] * 16, 32, 8, 128, 64, 0.5, 42, device="cuda", paged=False)
+        else:    # the two-tile kernel with one-tile items only (loose max_seqlen_q): the item ring laps group 1
+            lens = [100 + (11 * i) % 29 for i in range(64)]
+            b = varlen_batch(lens, lens, 32, 8, 128, 64, 0.5, 43, device="cuda", paged=False)
+            b.max_seqlen_q = 4096
         out = torch.empty_like(b.q)
         call = _varlen_call(b, out)
     else:

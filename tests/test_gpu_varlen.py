@@ -77,6 +77,43 @@ def test_prefill_pair_stale_nan_past_context(cuda):
     assert_attn_close(run_varlen(b), ref, "pair nan tail")
 
 
+def test_prefill_pair_single_tile_items_only(cuda):
+    """The two-tile kernel on a call whose every item has one query tile: 48 prompts of 100-128 tokens (5k rows at
+    32 heads, above the two-tile threshold) with a loose max_seqlen_q bound (4096), which the C ABI takes as "some
+    run may fill two tiles".  Softmax group 1 then skips every item, so the producer laps the 8-entry item ring
+    many times while group 1 only reads and releases entries: the ring's read barrier is what keeps the entries
+    valid.  Parity with the oracle and a clean device error word."""
+    from nvattn import _lib
+    lens = [100 + (7 * i) % 29 for i in range(48)]
+    b = batch(lens, lens, seed=24, paged=False)
+    b.max_seqlen_q = 4096
+    _lib.clear_device_error()
+    out = run_varlen(b, paged=False)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert_attn_close(out, ref_varlen(b, paged=False), "pair kernel, single-tile items")
+
+
+def test_varlen_padding_sequences_invariant(cuda):
+    """Batch padding in a mixed varlen step (the property the reference's scripts/check_padding.py:28-55 checks for
+    decode): appending empty sequences (no query rows, no keys, block-table rows of -1) leaves every real row's
+    output bitwise unchanged, on a mixed batch with decode rows, verify runs and prefill chunks."""
+    from nvattn import ops
+    q_lens = [1] * 40 + [5] * 8 + [300, 129]
+    k_lens = [60 + 53 * i for i in range(48)] + [300 + 256, 129 + 1000]
+    b = batch(q_lens, k_lens, seed=12)
+    alone = run_varlen(b)
+    pad = 6
+    cu_q = torch.cat([b.cu_seqlens_q, b.cu_seqlens_q[-1:].repeat(pad)])
+    cu_k = torch.cat([b.cu_seqlens_k, b.cu_seqlens_k[-1:].repeat(pad)])
+    bt = torch.cat([b.block_tables, torch.full((pad, b.block_tables.shape[1]), -1, dtype=torch.int32, device=cuda)])
+    padded = ops.flash_attn_varlen_func(b.q, b.k_cache, b.v_cache, max_seqlen_q=b.max_seqlen_q, cu_seqlens_q=cu_q,
+                                        max_seqlen_k=b.max_seqlen_k, cu_seqlens_k=cu_k, softmax_scale=b.scale,
+                                        causal=True, block_table=bt)
+    assert torch.equal(alone, padded)
+    assert_attn_close(alone, ref_varlen(b), "mixed batch before padding")
+
+
 @pytest.mark.parametrize("lens", [[700, 300], [1200, 1200, 1200, 1200]])
 def test_prefill_rising_scores_rescale_every_half_tile(cuda, lens):
     """Scores that rise along the keys: dim 0 of every query is 4 and dim 0 of key p gains 0.3 p, so each 64 keys

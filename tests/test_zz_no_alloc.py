@@ -3,12 +3,15 @@
 Such callers (an allocator hook or host callback where cudaMalloc would recurse or deadlock, a runtime that owns all
 memory through a fixed arena, an embedder without device allocation) cannot pass the workspace nva_paged_decode
 needs; this entry point keeps the split-KV partials in scratch compiled into the library instead.  The test calls it
-through the C ABI and checks it against nva_paged_decode within the attention tolerance, on two calls in a row.
+through the C ABI and checks it against nva_paged_decode and against the FP32 oracle within the attention tolerance,
+on two calls in a row.  The verify case includes a sequence shorter than its query run (3 keys, 5 query tokens):
+its first two rows see no key and must come out zero, as the oracle (flash-attn's semantics) gives them.
 
 The file name makes pytest collect it last, so a run that stops at the first failure has run every other test."""
 import pytest
 import torch
 
+import oracle
 from conftest import assert_attn_close
 
 pytestmark = pytest.mark.gpu
@@ -40,11 +43,14 @@ def test_noalloc_matches_workspace_entry_point(cuda, lens, n):
     B = b.num_seqs
     ref = ops.flash_attn_with_kvcache(b.q.view(B, n, 32, 128), b.k_cache, b.v_cache, cache_seqlens=b.context_lens,
                                       block_table=b.block_tables, softmax_scale=b.scale)
+    fp32 = oracle.paged_attention_ref(b.q.view(B, n, 32, 128).cpu(), b.k_cache.cpu(), b.v_cache.cpu(),
+                                      b.context_lens.cpu(), b.block_tables.cpu(), b.scale)
     for call in range(2):   # the second call reuses the scratch the first one left behind
         out = torch.full((B * n, 32, 128), float("nan"), dtype=torch.bfloat16, device=cuda)
         assert _noalloc(b, out) == 0, f"call {call}"
         torch.cuda.synchronize()
         assert_attn_close(out.view(B, n, 32, 128), ref, f"no-alloc call {call}")
+        assert_attn_close(out.view(B, n, 32, 128), fp32, f"no-alloc call {call} vs the oracle")
     assert _lib.device_error() == 0
 
 
