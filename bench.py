@@ -154,6 +154,24 @@ def decode_shard(world, rank, seed=0, B_per_gpu=64, k=0):
     return b, lens, H, KVH
 
 
+def decode_strong_shard(world, rank, seed=0):
+    """This rank's KV-head shard of BASELINE config 2 itself (64 sequences at every N): strong scaling over the
+    tensor-parallel head split, 32/N q heads and 8/N kv heads per rank."""
+    from nvattn.workloads import paged_decode_batch
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(512, 4097, (64,), generator=g).tolist()
+    H, KVH = 32 // world, 8 // world
+    b = paged_decode_batch(lens, 1, H, KVH, 128, 2048, 0.5, seed + 1 + rank, device="cuda", device_fill=True)
+    return b, lens, H, KVH
+
+
+def decode_kernel_name(n, H, KVH):
+    """The paged_decode_kernel<NP> instantiation a decode / verify call runs: the packed rows q_per_seq x group of
+    one kv head, padded to 16, 32 or 48 (decode_rows_padded in csrc/paged_decode.cu)."""
+    rows = n * (H // KVH)
+    return f"paged_decode_kernel<{next(x for x in (16, 32, 48) if rows <= x)}>"
+
+
 def attn_bytes(lens, n, H, KVH):
     from nvattn.workloads import bytes_decode
     return bytes_decode(lens, n, H, KVH)
@@ -307,6 +325,8 @@ def run_nvattn(args, world, rank, local):
                                      "us": round(v_ms * 1e3, 2),
                                      "TFLOPs": round(world * flops_decode(vl, k + 1, H) / (v_ms * 1e-3) / 1e12, 1)}
         del vb, vq, vout
+    if world > 1:
+        secondary["strong_tp"] = strong_row(world, rank, args, flush, pk)
     secondary.update(varlen_rows(world, rank, args, flush, pk))
     secondary["flash_attn_2_8_3_same_workloads"] = fa2_rows(world, rank, args, flush, b, q4, lens, H, KVH)
     from nvattn.workloads import accept_config
@@ -332,7 +352,7 @@ def run_nvattn(args, world, rank, local):
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e_ms, 5),
                 "api": "nvattn.attention.Attention.forward (CUDA-graph replay, inputs H2D from pinned memory, output D2H)"},
-        "roofline": {"kernel": "paged_decode_kernel<16>", "bound": "hbm",
+        "roofline": {"kernel": decode_kernel_name(1, H, KVH), "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": pk["hbm"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm"], 4), "peak_source": pk["source"],
                      "traffic": None if traffic is None else round(traffic),
@@ -340,12 +360,80 @@ def run_nvattn(args, world, rank, local):
         "gpu_launches": 2 * args.steps,   # per timed headline step: store_kvcache_kernel + paged_decode_kernel
         "secondary": secondary,
     }
+    if world == 1 and rank == 0 and not args.no_e2e_model:
+        del b, q4, out, flush
+        torch.cuda.empty_cache()
+        secondary["e2e_config5"] = e2e_model_rows(args)
     clocks = clk.summary()
     line["clocks"] = clocks
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.seed, budget_s=args.cpu_budget)
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def strong_row(world, rank, args, flush, pk):
+    """Strong scaling: BASELINE config 2's fixed batch of 64 sequences split over the N ranks by kv heads (at N = 8
+    one kv head, ~80 MB of KV per rank and step).  us = the slowest rank's decode launch; frac_per_rank = one rank's
+    algorithmic bytes / that time / measured HBM peak; GBps = all ranks' bytes / that time."""
+    from nvattn import ops
+    b, lens, H, KVH = decode_strong_shard(world, rank, args.seed)
+    q = b.q.view(b.num_seqs, 1, H, 128)
+    out = torch.empty_like(q)
+
+    def call():
+        ops.flash_attn_with_kvcache(q, b.k_cache, b.v_cache, cache_seqlens=b.context_lens,
+                                    block_table=b.block_tables, softmax_scale=b.scale, out=out)
+    t = time_steps(capture(call).replay, max(10, args.steps // 2), args.warmup, flush)
+    ms = max_over_ranks(statistics.mean(t), world)
+    by = attn_bytes(lens, 1, H, KVH)
+    return {"global_batch": 64, "per_rank_q_heads": H, "per_rank_kv_heads": KVH, "us": round(ms * 1e3, 2),
+            "MB_per_rank": round(by / 1e6, 1), "GBps": round(world * by / (ms * 1e-3) / 1e9, 1),
+            "frac_per_rank": round(by / (ms * 1e-3) / 1e9 / pk["hbm"], 3),
+            "hbm_floor_us": round(by / (pk["hbm"] * 1e9) * 1e6, 2)}
+
+
+def e2e_model_rows(args):
+    """BASELINE config 5 end to end (nvattn/e2e.py): random-init Qwen3-8B under the reference's own engine, greedy
+    n-gram speculative decoding with dynamic k over a fixed injected step-cost table, 64 requests of 1024 prompt
+    tokens, 256 new tokens each; the reference arm (its flash-attn 2.8.3 + Triton scatter) and this package's full
+    drop-in (attention, fused q/k-norm + rotary + scatter prologue, sharded greedy verify), each in its own process,
+    one after the other.  Output tokens / generate() wall time.  With random weights the model does not repeat its
+    own text, so n-gram guesses rarely fire; the second pair of rows lets the model guess for itself (every decode
+    step a k = 4 verify step, ~93% of guesses accepted)."""
+    import tempfile
+    rows = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        costs = os.path.join(tmp, "costs.json")
+        model = os.path.join(tmp, "qwen3_8b_random")
+        env = dict(os.environ, PYTHONPATH=os.path.join(REPO, "nano-vllm-spec-decode_b200"))
+        for variant, extra in (("spec_ngram_dynk_graph", ["--step-costs", costs, "--synthetic-step-costs"]),
+                               ("spec_draft_graph", ["--max-num-seqs", "64"])):
+            for arm in ("reference", "nvattn+all"):
+                out = os.path.join(tmp, f"{variant}_{arm}.json")
+                cmd = [sys.executable, "-m", "nvattn.e2e", "--arm", arm, "--variant", variant, "--model-dir", model,
+                       "--out", out] + extra
+                try:
+                    r = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
+                except subprocess.TimeoutExpired:
+                    rows[f"{variant}/{arm}"] = {"unavailable": "timed out after 600 s"}
+                    continue
+                if r.returncode != 0:
+                    rows[f"{variant}/{arm}"] = {"unavailable": (r.stderr.strip().splitlines() or ["failed"])[-1][:200]}
+                    continue
+                with open(out) as f:
+                    d = json.load(f)
+                spec = d.get("spec") or {}
+                rows[f"{variant}/{arm}"] = {
+                    "output_tok_per_s": round(d["output_tok_per_s"], 1), "generate_s": round(d["generate_s"], 3),
+                    "output_tokens": d["output_tokens"], "k_steps": spec.get("k_steps"),
+                    "accepted": spec.get("num_accepted"), "drafts": spec.get("num_drafts"),
+                    "device_error": d.get("device_error")}
+            ref, own = rows.get(f"{variant}/reference", {}), rows.get(f"{variant}/nvattn+all", {})
+            if "output_tok_per_s" in ref and "output_tok_per_s" in own:
+                rows[f"{variant}/speedup"] = round(own["output_tok_per_s"] / ref["output_tok_per_s"], 3)
+    rows["workload"] = "64 requests x 1024-token seeded prompts (128-token span repeated 4x), 256 new tokens, T=0"
+    return rows
 
 
 def prefill_flops(q_lens, k_lens, H, D=128):
@@ -568,6 +656,7 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e-model", action="store_true", help="skip the config-5 end-to-end rows (N = 1 only)")
     ap.add_argument("--profile-case", choices=["decode", "verify8", "prefill4", "prefill16k", "mixed4"],
                     help="run one workload --steps times on one GPU (for ncu captures) and exit")
     args = ap.parse_args()

@@ -121,6 +121,27 @@ NVA_API int nva_greedy_accept(const void* target_ids, int64_t target_row_stride,
                               int32_t id_bytes, void* num_accepted, void* next_tokens, void* stream);
 
 /*
+ * Qwen3's attention prologue in one pass.  Replaces, for every token, the q / k RMSNorm and rotary embedding of
+ * Qwen3Attention.pre_attn (nanovllm/models/qwen3.py:88-97, layers/layernorm.py:16-26,
+ * layers/rotary_embedding.py:6-14 and 37-48) and the KV scatter of Attention.forward (layers/attention.py:61-62):
+ *   qkv [T, (H + 2 KVH) * D] bf16 (q heads, then k heads, then v heads; row stride in elements), positions [T] int64,
+ *   cos_sin [max_position, D] float32 (cos of position p in columns [0, D/2), sin in [D/2, D)),
+ *   q_norm_weight, k_norm_weight [D] bf16 ->
+ *   q_out [T, H, D]:   rope(bf16(bf16(q * rsqrt(mean(q^2) + eps)) * q_norm_weight))
+ *   k' (same with k_norm_weight), stored to k_out [T, KVH, D] when k_out != NULL,
+ *   k_cache / v_cache rows (the nva_store_kvcache layout) at slot = slot_mapping[t] of k' and of v, when
+ *   slot_mapping != NULL; slot -1 is skipped, slots past num_slots are skipped and set bit 1 of the error word.
+ * rope: x1 = dims [0, D/2), x2 = dims [D/2, D): (x1 cos - x2 sin, x2 cos + x1 sin) in float32, rounded to bf16.
+ * head_dim 128.  Positions outside [0, max_position) are clamped.
+ */
+NVA_API int nva_qk_norm_rope_store(const void* qkv, int64_t qkv_row_stride, int32_t num_tokens, int32_t num_heads,
+                                   int32_t num_kv_heads, int32_t head_dim, const int64_t* positions,
+                                   const float* cos_sin, int32_t max_position, const void* q_norm_weight,
+                                   const void* k_norm_weight, float eps, void* q_out, int64_t q_out_row_stride,
+                                   void* k_out, int64_t k_out_row_stride, void* k_cache, void* v_cache,
+                                   int64_t num_slots, const int32_t* slot_mapping, void* stream);
+
+/*
  * Greedy verify from vocabulary shards.  Replaces, for all-greedy verify steps, the logits gather to rank 0 in
  * ParallelLMHead.forward (nanovllm/layers/embed_head.py:56-68) and the argmax + accept rule of verify_drafts
  * (nanovllm/layers/sampler.py:66-82).

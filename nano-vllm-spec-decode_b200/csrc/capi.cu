@@ -349,6 +349,37 @@ NVA_API int nva_greedy_accept(const void* target_ids, int64_t target_row_stride,
   return e == cudaSuccess ? NVA_OK : cuda_fail(e);
 }
 
+NVA_API int nva_qk_norm_rope_store(const void* qkv, int64_t qkv_row_stride, int32_t num_tokens, int32_t num_heads,
+                                   int32_t num_kv_heads, int32_t head_dim, const int64_t* positions,
+                                   const float* cos_sin, int32_t max_position, const void* q_norm_weight,
+                                   const void* k_norm_weight, float eps, void* q_out, int64_t q_out_row_stride,
+                                   void* k_out, int64_t k_out_row_stride, void* k_cache, void* v_cache,
+                                   int64_t num_slots, const int32_t* slot_mapping, void* stream) {
+  if (num_tokens < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_position <= 0 || num_slots < 0)
+    return NVA_ERR_INVALID_ARGUMENT;
+  if (head_dim != nva::kHeadDim) return NVA_ERR_UNSUPPORTED;
+  if (num_tokens == 0) return NVA_OK;
+  if (qkv == nullptr || positions == nullptr || cos_sin == nullptr || q_norm_weight == nullptr ||
+      k_norm_weight == nullptr || q_out == nullptr)
+    return NVA_ERR_INVALID_ARGUMENT;
+  if (slot_mapping != nullptr && (k_cache == nullptr || v_cache == nullptr)) return NVA_ERR_INVALID_ARGUMENT;
+  const int64_t width = static_cast<int64_t>(num_heads + 2 * num_kv_heads) * head_dim;
+  if (qkv_row_stride < width || q_out_row_stride < static_cast<int64_t>(num_heads) * head_dim ||
+      (k_out != nullptr && k_out_row_stride < static_cast<int64_t>(num_kv_heads) * head_dim))
+    return NVA_ERR_INVALID_ARGUMENT;
+  // 8-byte vectors (4 bf16) everywhere, 16-byte float4 reads of the cos / sin table
+  auto al8 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
+  if (!al8(qkv) || qkv_row_stride % 4 != 0 || !al8(q_out) || q_out_row_stride % 4 != 0 || !aligned16(cos_sin) ||
+      (k_out != nullptr && (!al8(k_out) || k_out_row_stride % 4 != 0)) ||
+      (k_cache != nullptr && (!al8(k_cache) || !al8(v_cache))) || !al8(q_norm_weight) || !al8(k_norm_weight))
+    return NVA_ERR_ALIGNMENT;
+  cudaError_t e = nva::launch_qk_prologue(qkv, qkv_row_stride, num_tokens, num_heads, num_kv_heads, positions, cos_sin,
+                                          max_position, q_norm_weight, k_norm_weight, eps, q_out, q_out_row_stride,
+                                          k_out, k_out_row_stride, k_cache, v_cache, num_slots, slot_mapping,
+                                          static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? NVA_OK : cuda_fail(e);
+}
+
 NVA_API int nva_shard_argmax(const void* logits, int64_t row_stride, int32_t rows, int32_t vocab_shard,
                              int64_t vocab_offset, int32_t elem_bytes, uint64_t* keys, void* stream) {
   if (rows < 0 || vocab_shard < 0 || vocab_offset < 0) return NVA_ERR_INVALID_ARGUMENT;

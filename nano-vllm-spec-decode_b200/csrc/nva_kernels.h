@@ -134,6 +134,13 @@ cudaError_t launch_greedy_accept(const void* target, int64_t target_row_stride, 
 int cuda_fail(cudaError_t e);
 int encode_rows(CUtensorMap* tm, const void* base, int64_t heads, int64_t rows, int64_t row_stride_bytes);
 
+// Qwen3's attention prologue in one pass (q/k RMSNorm, rotary, KV scatter); see qk_prologue.cu.
+cudaError_t launch_qk_prologue(const void* qkv, int64_t qkv_stride, int32_t T, int32_t H, int32_t KVH,
+                               const int64_t* positions, const float* cos_sin, int32_t max_pos, const void* q_w,
+                               const void* k_w, float eps, void* q_out, int64_t q_out_stride, void* k_out,
+                               int64_t k_out_stride, void* k_cache, void* v_cache, int64_t num_slots,
+                               const int32_t* slots, cudaStream_t stream);
+
 // Per-row (max, index) keys of a vocabulary shard of logits (bf16 when elem_bytes == 2, float when 4), and the merge
 // of several shards' keys into greedy accept lengths; see shard_argmax.cu.
 cudaError_t launch_shard_argmax(const void* logits, int64_t row_stride, int32_t rows, int32_t vocab,

@@ -24,6 +24,8 @@ SIGNATURES = {
                                             _P]),
     "nva_varlen_workspace_bytes": (ctypes.c_size_t, [_I32, _I32, _I32, _I32, _I32]),
     "nva_greedy_accept": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _I32, _I32, _I32, _P, _P, _P]),
+    "nva_qk_norm_rope_store": (ctypes.c_int, [_P, _I64, _I32, _I32, _I32, _I32, _P, _P, _I32, _P, _P, _F, _P, _I64,
+                                              _P, _I64, _P, _P, _I64, _P, _P]),
     "nva_shard_argmax": (ctypes.c_int, [_P, _I64, _I32, _I32, _I64, _I32, _P, _P]),
     "nva_shard_accept": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _I64, _P, _I32, _P, _P, _P]),
     "nva_paged_decode_noalloc": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _P, _I32, _I32, _I32, _I32, _I32,

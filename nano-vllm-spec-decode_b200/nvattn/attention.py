@@ -33,6 +33,14 @@ class Attention(nn.Module):
         k_cache, v_cache = self.k_cache, self.v_cache
         if k_cache.numel() and v_cache.numel():
             ops.store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
+        return self.forward_stored(q, k, v)
+
+    def forward_stored(self, q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | None):
+        """forward() for a step whose K/V rows are already in the cache (written by the fused prologue,
+        ops.qk_norm_rope_store).  k and v are read only by a prefill without a block table (contiguous K/V);
+        otherwise they may be None."""
+        context = get_context()
+        k_cache, v_cache = self.k_cache, self.v_cache
         if context.is_prefill:
             if context.block_tables is not None:    # prefix cache / chunked prefill / mixed batch
                 k, v = k_cache, v_cache

@@ -5,6 +5,8 @@ dynamic k), with the attention of one of two arms:
   reference   the unmodified reference: flash-attn 2.8.3 + its Triton KV scatter (nanovllm/layers/attention.py)
   nvattn      this package swapped in by nvattn.nanovllm_dropin.install_attention
   nvattn+argmax  the same, plus nanovllm_dropin.install_greedy_argmax (greedy verify from per-rank (max, index) pairs)
+  nvattn+all  the same, plus nanovllm_dropin.install_fused_prologue (q / k norm + rotary + KV scatter in one kernel)
+              and install_mixed_step_graph (whole mixed steps as one CUDA graph)
 
 At tensor_parallel_size > 1 both arms also get nanovllm_dropin.install_tp_speculative (the reference refuses
 speculative decoding with TP > 1, config.py:39-41).
@@ -64,7 +66,7 @@ VARIANTS = {
     "mixed_spec_ngram_graph": dict(enforce_eager=False, enable_mixed_batching=True, max_num_batched_tokens=256,
                                    speculative_method="ngram", num_speculative_tokens=4),
 }
-ARMS = ("reference", "nvattn", "nvattn+argmax")
+ARMS = ("reference", "nvattn", "nvattn+argmax", "nvattn+all")
 
 ENV_ARM, ENV_TP, ENV_COSTS, ENV_SEED = "NVA_E2E_ARM", "NVA_E2E_TP", "NVA_E2E_STEP_COSTS", "NVA_E2E_WEIGHT_SEED"
 
@@ -208,8 +210,11 @@ def _apply_from_env() -> None:
         nanovllm_dropin.install_tp_speculative()
     if arm.startswith("nvattn"):
         nanovllm_dropin.install_attention()
-    if arm == "nvattn+argmax":
+    if arm in ("nvattn+argmax", "nvattn+all"):
         nanovllm_dropin.install_greedy_argmax()
+    if arm == "nvattn+all":
+        nanovllm_dropin.install_fused_prologue()
+        nanovllm_dropin.install_mixed_step_graph()
     costs_file = os.environ.get(ENV_COSTS)
     if costs_file and os.path.exists(costs_file):
         with open(costs_file) as f:

@@ -30,6 +30,26 @@ install_greedy_argmax()
     go to the lowest vocabulary index, as torch's argmax over the concatenated logits does, so the result is the
     reference's bit for bit.
 
+install_fused_prologue()
+    Qwen3's attention prologue in one kernel (`nva_qk_norm_rope_store`): the q / k RMSNorm and rotary embedding of
+    Qwen3Attention.pre_attn (nanovllm/models/qwen3.py:88-97) and the KV scatter of Attention.forward
+    (attention.py:61-62) become one pass over the projection output.  Qwen3Attention.forward (whole-model steps:
+    prefill, decode / verify and their CUDA graphs) scatters in the same kernel; pre_attn (the piecewise segments of
+    mixed steps, recorded without a Context) fuses the norms and rotary only and leaves the scatter to the
+    attention call, as the reference does.  Needs install_attention.
+
+install_mixed_step_graph()
+    Mixed steps (enable_mixed_batching with mixed_cuda_graph) as one CUDA graph per token bucket.  The reference
+    records the L + 1 segments between the attentions as separate graphs and runs every attention eagerly in
+    between (ModelRunner.run_piecewise, model_runner.py:563-589, 677-687), because flash-attn's varlen call reads
+    host values of the step's batch.  nvattn's varlen attention reads its batch layout from device memory only and
+    keeps a fixed launch geometry for a fixed sequence capacity, so the whole step -- segments and attentions -- is
+    recorded once per bucket over static Context buffers (cu_seqlens for max_num_seqs sequences, padded with empty
+    ones; the slot mapping padded with -1; a max_num_seqs x max_num_blocks block table) and replayed after the step's
+    Context is copied into them.  Rows of the bucket past the step's tokens belong to no sequence: attention neither
+    reads nor writes them, and nothing else mixes rows.  Steps the graphs do not cover (more sequences than
+    max_num_seqs, or eager mode) take the reference's path.  Needs install_attention.
+
 Each function is idempotent and must run in every process that builds a model: in the TP worker processes too
 (they are started with multiprocessing's spawn, which imports the parent's main module first; call these at module
 level there, as nvattn.e2e does).
@@ -193,3 +213,120 @@ def install_greedy_argmax() -> None:
 
     mr.ModelRunner.run_verify = runner_run_verify
     _installed.add("greedy_argmax")
+
+
+def install_fused_prologue() -> None:
+    """q / k RMSNorm + rotary (+ the KV scatter in whole-model steps) in one kernel (see module docstring)."""
+    if "fused_prologue" in _installed:
+        return
+    assert "attention" in _installed, "install_attention first"
+    from nanovllm.models import qwen3
+    from nanovllm.utils.context import get_context
+    from . import ops
+
+    def prologue(self, positions, hidden_states, scatter):
+        qkv = self.qkv_proj(hidden_states)
+        attn = self.attn
+        ctx = get_context() if scatter else None
+        cache = scatter and attn.k_cache.numel() > 0
+        contiguous_kv = not scatter or (ctx.is_prefill and ctx.block_tables is None)
+        q, k, v = ops.qk_norm_rope_store(
+            qkv, positions, self.rotary_emb.cos_sin_cache, self.q_norm.weight, self.k_norm.weight, self.q_norm.eps,
+            self.num_heads, self.num_kv_heads, attn.k_cache if cache else None, attn.v_cache if cache else None,
+            ctx.slot_mapping if cache else None, want_k=contiguous_kv)
+        return q, k, v
+
+    def attention_forward(self, positions, hidden_states):
+        assert not self.qkv_bias, "the fused prologue is Qwen3's (q / k norms, no qkv bias)"
+        q, k, v = prologue(self, positions, hidden_states, True)
+        o = self.attn.forward_stored(q, k, v)
+        return self.post_attn(o)
+
+    def attention_pre_attn(self, positions, hidden_states):
+        assert not self.qkv_bias, "the fused prologue is Qwen3's (q / k norms, no qkv bias)"
+        return prologue(self, positions, hidden_states, False)
+
+    qwen3.Qwen3Attention.forward = attention_forward
+    qwen3.Qwen3Attention.pre_attn = attention_pre_attn
+    _installed.add("fused_prologue")
+
+
+def install_mixed_step_graph() -> None:
+    """Whole mixed steps (segments + attentions) as one CUDA graph per token bucket (see module docstring)."""
+    if "mixed_step_graph" in _installed:
+        return
+    assert "attention" in _installed, "install_attention first"
+    import torch
+    from nanovllm.engine import model_runner as mr
+    from nanovllm.utils.context import get_context, set_context, reset_context
+
+    capture_cudagraph = mr.ModelRunner.capture_cudagraph
+    run_piecewise = mr.ModelRunner.run_piecewise
+
+    def whole_step(self, n):
+        layers = self.model.model.layers
+        pv = self.piecewise_vars
+        for i in range(len(layers) + 1):
+            if i:
+                pv["o"][:n] = layers[i - 1].self_attn.attn(pv["q"][:n], pv["k"][:n], pv["v"][:n])
+            self.run_segment(i, n)
+
+    @torch.inference_mode()
+    def runner_capture_cudagraph(self):
+        capture_cudagraph(self)
+        self.mixed_step_graphs = {}
+        if not self.mixed_buckets:
+            return
+        S, N = self.config.max_num_seqs, self.mixed_buckets[-1]
+        sv = dict(cu_q=torch.zeros(S + 1, dtype=torch.int32), cu_k=torch.zeros(S + 1, dtype=torch.int32),
+                  slots=torch.full((N,), -1, dtype=torch.int32),
+                  bt=torch.full((S, self.max_num_blocks), -1, dtype=torch.int32))
+        self.mixed_step_vars = sv
+        for n in reversed(self.mixed_buckets):
+            # recorded with every sequence empty; max_seqlen_q = n is an upper bound for any step of this bucket
+            set_context(True, sv["cu_q"], sv["cu_k"], n, self.config.max_model_len, sv["slots"][:n], None, sv["bt"])
+            whole_step(self, n)    # warmup
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, self.graph_pool):
+                whole_step(self, n)
+            self.mixed_step_graphs[n] = graph
+            reset_context()
+        torch.cuda.synchronize()
+
+    @torch.inference_mode()
+    def runner_run_piecewise(self, input_ids, positions):
+        graphs = getattr(self, "mixed_step_graphs", None)
+        ctx = get_context()
+        n = input_ids.size(0)
+        B = ctx.cu_seqlens_q.numel() - 1
+        if self.enforce_eager or not graphs or B > self.config.max_num_seqs or n > self.mixed_buckets[-1]:
+            return run_piecewise(self, input_ids, positions)
+        bucket = next(x for x in self.mixed_buckets if x >= n)
+        pv, sv = self.piecewise_vars, self.mixed_step_vars
+        pv["input_ids"][:n] = input_ids
+        pv["input_ids"][n:bucket] = 0
+        pv["positions"][:n] = positions
+        pv["positions"][n:bucket] = 0
+        pv["o"][n:bucket] = 0
+        for name, src in (("cu_q", ctx.cu_seqlens_q), ("cu_k", ctx.cu_seqlens_k)):
+            sv[name][:B + 1] = src
+            sv[name][B + 1:] = src[-1:]      # empty sequences after the last one
+        sv["slots"][:n] = ctx.slot_mapping
+        sv["slots"][n:bucket] = -1
+        W = ctx.block_tables.size(1)
+        if W > sv["bt"].size(1):
+            return run_piecewise(self, input_ids, positions)
+        sv["bt"][:B, :W] = ctx.block_tables
+        graphs[bucket].replay()
+        return pv["hidden"][:n]
+
+    exit_runner = mr.ModelRunner.exit
+
+    def runner_exit(self):
+        self.mixed_step_graphs = {}    # released before the graph pool, as the reference releases its own graphs
+        exit_runner(self)
+
+    mr.ModelRunner.capture_cudagraph = runner_capture_cudagraph
+    mr.ModelRunner.run_piecewise = runner_run_piecewise
+    mr.ModelRunner.exit = runner_exit
+    _installed.add("mixed_step_graph")

@@ -221,3 +221,40 @@ def shard_accept(keys: torch.Tensor, draft_ids: torch.Tensor, num_drafts: torch.
         keys.data_ptr(), num_shards, S, K, draft_ids.data_ptr() if K else 0, draft_ids.stride(0) if K else 0,
         num_drafts.data_ptr(), draft_ids.element_size(), acc.data_ptr(), nxt.data_ptr(), _stream()), "shard accept")
     return acc, nxt
+
+
+def qk_norm_rope_store(qkv: torch.Tensor, positions: torch.Tensor, cos_sin_cache: torch.Tensor,
+                       q_norm_weight: torch.Tensor, k_norm_weight: torch.Tensor, eps: float, num_heads: int,
+                       num_kv_heads: int, k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,
+                       slot_mapping: torch.Tensor | None = None, want_k: bool = False):
+    """Qwen3's attention prologue in one kernel: from the fused projection output qkv [T, (H + 2 KVH) * 128], the
+    normalised and rotated q [T, H, 128] (returned), the same for k (returned when want_k, else None), and, with a
+    cache, k and v scattered to slot_mapping's slots (qwen3.py:88-97 then attention.py:61-62).  cos_sin_cache is the
+    reference RotaryEmbedding's [max_position, 1 or none, 128] float32 table.  Returns (q, k, v) with v a view of
+    qkv, as Qwen3Attention.pre_attn returns them."""
+    _need_cuda(qkv, positions, cos_sin_cache, q_norm_weight, k_norm_weight)
+    D = 128
+    T = qkv.shape[0]
+    assert qkv.dim() == 2 and qkv.shape[1] == (num_heads + 2 * num_kv_heads) * D and qkv.stride(1) == 1
+    assert qkv.dtype == torch.bfloat16 and q_norm_weight.dtype == k_norm_weight.dtype == torch.bfloat16
+    assert positions.dtype == torch.int64 and positions.is_contiguous() and positions.numel() == T
+    table = cos_sin_cache.reshape(-1, D)
+    assert table.dtype == torch.float32 and table.is_contiguous()
+    q = torch.empty(T, num_heads, D, dtype=qkv.dtype, device=qkv.device)
+    k = torch.empty(T, num_kv_heads, D, dtype=qkv.dtype, device=qkv.device) if want_k else None
+    if slot_mapping is not None:
+        _need_cuda(k_cache, v_cache, slot_mapping)
+        assert slot_mapping.dtype == torch.int32 and slot_mapping.is_contiguous() and slot_mapping.numel() == T
+        assert k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.dtype == qkv.dtype
+        assert k_cache.stride(1) == num_kv_heads * D
+        num_slots = k_cache.numel() // (num_kv_heads * D)
+    else:
+        num_slots = 0
+    _lib.check(_lib.load().nva_qk_norm_rope_store(
+        qkv.data_ptr(), qkv.stride(0), T, num_heads, num_kv_heads, D, positions.data_ptr(), table.data_ptr(),
+        table.shape[0], q_norm_weight.data_ptr(), k_norm_weight.data_ptr(), float(eps), q.data_ptr(), q.stride(0),
+        k.data_ptr() if k is not None else 0, k.stride(0) if k is not None else 0,
+        k_cache.data_ptr() if slot_mapping is not None else 0, v_cache.data_ptr() if slot_mapping is not None else 0,
+        num_slots, slot_mapping.data_ptr() if slot_mapping is not None else 0, _stream()), "qk norm rope store")
+    v = qkv[:, (num_heads + num_kv_heads) * D:].view(T, num_kv_heads, D)
+    return q, k, v

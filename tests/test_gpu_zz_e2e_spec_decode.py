@@ -4,15 +4,18 @@ speculative decoding of a random-init Qwen3-8B (BASELINE config 5's model and pr
 on the same seeds.  Drafts come from the n-gram proposer (config 5's method; with random weights the model rarely
 repeats itself within 48 tokens, so these runs are mostly plain decode steps) and from the model guessing for
 itself (the reference's spec_draft variants: nearly every guess accepted, so every decode step is a k = 4 verify
-step), plus a mixed-batching run (decode requests and prefill chunks in one step, piecewise CUDA graphs).
+step), plus mixed-batching runs (decode requests and prefill chunks in one step).  Arms: the reference; nvattn's
+attention alone (nvattn); with the sharded greedy verify (nvattn+argmax); and the whole drop-in (nvattn+all: also
+the fused q/k-norm + rotary + KV-scatter prologue, and mixed steps recorded as one CUDA graph each).
 
 Checks, following the reference's tests/test_greedy.py (the method and its 0.5 tolerance, :1-30, 244-248):
   * every run's tokens face a float32 referee (tests/e2e_referee.py): each generated token must be the referee's
     top-1 or within 0.5 of its top-1 logit;
   * runs that compute exactly the same thing must give identical tokens: CUDA-graph vs eager steps with nvattn
-    (the reference's MUST_MATCH pairs), and nvattn with and without the per-rank (max, index) greedy verify (which
-    is bit-exact by construction);
-  * self-drafting accepts at least 90% of the tested guesses in both arms (a wrong verify attention would reject
+    (the reference's MUST_MATCH pairs; with nvattn+all the graph side is the whole-step mixed graph, the eager side
+    the reference's segment-by-segment path), and nvattn with and without the per-rank (max, index) greedy verify
+    (which is bit-exact by construction);
+  * self-drafting accepts at least 85% of the tested guesses in both arms (a wrong verify attention would reject
     guesses the draft pass, which shares no state with it, agrees on); the device error word of the nvattn kernels
     stays 0; the mixed run did run mixed steps.
 Where the nvattn arm and the reference arm part ways, the first diverging position of each request is printed
@@ -43,10 +46,18 @@ RUNS = [                  # (name, arm, variant)
     ("nva_draft_eager", "nvattn", "spec_draft"),
     ("nva_argmax_draft_graph", "nvattn+argmax", "spec_draft_graph"),
     ("nva_mixed_graph", "nvattn", "mixed_graph"),
+    ("nva_mixed_eager", "nvattn", "mixed_eager"),
+    ("all_draft_graph", "nvattn+all", "spec_draft_graph"),
+    ("all_mixed_graph", "nvattn+all", "mixed_graph"),
+    ("all_mixed_eager", "nvattn+all", "mixed_eager"),
 ]
 MUST_MATCH = {"nva_spec_eager": "nva_spec_graph", "nva_draft_eager": "nva_draft_graph",
-              "nva_argmax_draft_graph": "nva_draft_graph"}
-MIN_ACCEPTANCE = 0.9      # a model guessing for itself (the reference's test_greedy.py uses 0.95 on real weights)
+              "nva_argmax_draft_graph": "nva_draft_graph", "nva_mixed_eager": "nva_mixed_graph",
+              "all_mixed_eager": "all_mixed_graph"}
+# A model guessing for itself: the guesses come from the same weights with other batch shapes, so only bf16
+# near-ties reject one (0.92-0.93 measured in both arms with these random weights; the reference's test_greedy.py
+# asks 0.95 of real weights).  A wrong verify attention rejects far more.
+MIN_ACCEPTANCE = 0.85
 
 
 def _reference_available() -> bool:
@@ -113,10 +124,11 @@ def test_spec_decode_end_to_end(tmp_path):
     for name, partner in MUST_MATCH.items():
         same = sum(first_diff(a, b) is None for a, b in zip(runs[partner], runs[name]))
         assert same == NUM_PROMPTS, f"{name} differs from {partner} on {NUM_PROMPTS - same} of {NUM_PROMPTS} requests"
-    for name in ("ref_draft_graph", "nva_draft_graph", "nva_draft_eager", "nva_argmax_draft_graph"):
+    for name in ("ref_draft_graph", "nva_draft_graph", "nva_draft_eager", "nva_argmax_draft_graph", "all_draft_graph"):
         s = results[name]["spec"]
         rate = s["num_accepted"] / max(s["num_accepted"] + s["num_rejected"], 1)
         assert s["num_drafts"] > 0 and rate >= MIN_ACCEPTANCE, f"{name}: acceptance {rate:.3f} of {s['num_drafts']}"
-    assert results["nva_mixed_graph"]["mixed_steps"] > 0, "no mixed step ran"
+    for name in ("nva_mixed_graph", "all_mixed_graph"):
+        assert results[name]["mixed_steps"] > 0, f"{name}: no mixed step ran"
     for d in divergences:
         assert d["reference_gap"] <= TOL and d["nvattn_gap"] <= TOL
