@@ -309,7 +309,9 @@ def run_nvattn(args, world, rank, local):
     # ---- secondary rows: verify (config 3) and greedy accept at this N
     secondary = {}
     for k in (1, 2, 4, 8):
-        vb, vl, _, _ = decode_shard(world, rank, args.seed + 10 + k, B_per_gpu=32, k=k)
+        # one batch of contexts for every k (B = 32, contexts U[256, 2048]), so the k rows differ
+        # only in their query tokens
+        vb, vl, _, _ = decode_shard(world, rank, args.seed + 10, B_per_gpu=32, k=k)
         vq = vb.q.view(vb.num_seqs, k + 1, H, 128)
         vout = torch.empty_like(vq)
 
@@ -327,6 +329,8 @@ def run_nvattn(args, world, rank, local):
         del vb, vq, vout
     if world > 1:
         secondary["strong_tp"] = strong_row(world, rank, args, flush, pk)
+    else:
+        secondary.update(aux_rows(args, flush, pk))
     secondary.update(varlen_rows(world, rank, args, flush, pk))
     secondary["flash_attn_2_8_3_same_workloads"] = fa2_rows(world, rank, args, flush, b, q4, lens, H, KVH)
     from nvattn.workloads import accept_config
@@ -599,15 +603,67 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def aux_kernel_call(case, seed):
+    """The two kernels around attention, on workloads larger than L2 (HBM-bound, one pass each):
+      argmax    nva_shard_argmax + nva_shard_accept on the largest k = 4 verify step of config 3's shape: 510 rows
+                (102 sequences x 5) of 151936 bf16 logits (155 MB), whole vocabulary on one GPU;
+      prologue  nva_qk_norm_rope_store on an 8192-token prefill chunk of Qwen3-8B (qkv 8192 x 6144 bf16 in; q, the
+                cache rows of k and v out).
+    Returns (call, algorithmic bytes per call)."""
+    from nvattn import ops
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    if case == "argmax":
+        S, k, V = 102, 4, 151936
+        logits = (torch.randn(S * (k + 1), V, generator=g, device="cuda") * 1.3).to(torch.bfloat16)
+        drafts = torch.randint(0, V, (S, k), generator=g, device="cuda")
+        nd = torch.full((S,), k, dtype=torch.int64, device="cuda")
+
+        def call():
+            keys = ops.shard_argmax(logits, 0)
+            ops.shard_accept(keys.view(1, S, k + 1), drafts, nd)
+        return call, logits.numel() * 2 + S * (k + 1) * 8 * 2
+    T, H, KVH, D = 8192, 32, 8, 128
+    qkv = (torch.randn(T, (H + 2 * KVH) * D, generator=g, device="cuda")).to(torch.bfloat16)
+    pos = torch.arange(T, device="cuda", dtype=torch.int64)
+    inv_freq = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float32, device="cuda") / D))
+    angles = torch.arange(T, dtype=torch.float32, device="cuda")[:, None] * inv_freq[None, :]
+    table = torch.cat((angles.cos(), angles.sin()), dim=-1).contiguous()    # RotaryEmbedding's cos / sin rows
+    w = torch.ones(D, dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros(T // 256, 256, KVH, D, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(T, generator=g, device="cuda").to(torch.int32)
+
+    def call():
+        ops.qk_norm_rope_store(qkv, pos, table, w, w, 1e-6, H, KVH, kc, vc, slots)
+    # read qkv (+ positions, slots), write q and the k / v cache rows; the cos / sin rows read once per token
+    return call, qkv.numel() * 2 + T * H * D * 2 + 2 * T * KVH * D * 2 + T * (8 + 4 + D * 4)
+
+
+def aux_rows(args, flush, pk):
+    """Secondary rows of the kernels around attention (aux_kernel_call): device time of one call, algorithmic
+    GB/s, fraction of the measured HBM peak."""
+    rows = {}
+    for case, name in (("argmax", "shard_argmax_accept_510x151936"), ("prologue", "qk_prologue_8192_tokens")):
+        call, by = aux_kernel_call(case, args.seed)
+        t = time_steps(capture(call).replay, max(10, args.steps // 2), args.warmup, flush)
+        ms = statistics.mean(t)
+        rows[name] = {"us": round(ms * 1e3, 2), "GBps": round(by / (ms * 1e-3) / 1e9, 1),
+                      "frac_hbm": round(by / (ms * 1e-3) / 1e9 / pk["hbm"], 3), "MB": round(by / 1e6, 1)}
+        del call
+    return rows
+
+
 def profile_case(args):
     """One workload launched `--steps` times (after `--warmup` launches) and nothing else: the command the ncu
     summaries under profiles/ capture.  Prints the mean device time per launch (CUDA events, no L2 flush)."""
     from nvattn import ops
     from nvattn.workloads import mixed_config, varlen_batch
     case = args.profile_case
-    if case in ("decode", "verify8"):
-        k = 0 if case == "decode" else 8
-        b, _, H, KVH = decode_shard(1, 0, args.seed if k == 0 else args.seed + 10 + k, B_per_gpu=64 if k == 0 else 32,
+    if case in ("argmax", "prologue"):
+        call = aux_kernel_call(case, args.seed)[0]
+    elif case in ("decode", "verify4", "verify8"):
+        k = 0 if case == "decode" else int(case[len("verify"):])
+        b, _, H, KVH = decode_shard(1, 0, args.seed if k == 0 else args.seed + 10, B_per_gpu=64 if k == 0 else 32,
                                     k=k)
         q = b.q.view(b.num_seqs, k + 1, H, 128)
         out = torch.empty_like(q)
@@ -657,7 +713,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e-model", action="store_true", help="skip the config-5 end-to-end rows (N = 1 only)")
-    ap.add_argument("--profile-case", choices=["decode", "verify8", "prefill4", "prefill16k", "mixed4"],
+    ap.add_argument("--profile-case", choices=["decode", "verify4", "verify8", "prefill4", "prefill16k", "mixed4",
+                                               "argmax", "prologue"],
                     help="run one workload --steps times on one GPU (for ncu captures) and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

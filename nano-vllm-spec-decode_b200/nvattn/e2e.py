@@ -11,6 +11,9 @@ dynamic k), with the attention of one of two arms:
 At tensor_parallel_size > 1 both arms also get nanovllm_dropin.install_tp_speculative (the reference refuses
 speculative decoding with TP > 1, config.py:39-41).
 
+Reproducibility: torch.compile's Inductor is set to deterministic mode in every arm (no kernel configs chosen by
+timing), so repeated runs of a variant give the same tokens.
+
 What stands in for what the reference would load (no checkpoint, tokenizer or network here):
   * the model directory holds only a config.json with Qwen3-8B's published shape (36 layers, hidden 4096,
     32 q / 8 kv heads of 128, SwiGLU 12288, vocab 151936, RoPE theta 1e6, bf16);
@@ -201,6 +204,11 @@ def _apply_from_env() -> None:
     pkg = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     if pkg not in sys.path:
         sys.path.insert(0, pkg)
+    # torch.compile (RMSNorm, rotary, SiluAndMul, Sampler) otherwise picks some Triton kernel configs by timing them
+    # at run time, so two processes running the same variant can round differently (seen as different tokens, the
+    # reference arm included); with this set, every process compiles the same kernels.  It applies to every arm.
+    import torch._inductor.config
+    torch._inductor.config.deterministic = True
     import nanovllm.engine.model_runner as mr
     import nanovllm.engine.llm_engine as le
     from nvattn import nanovllm_dropin
@@ -224,9 +232,38 @@ def _apply_from_env() -> None:
         mr.ModelRunner.measure_step_costs = lambda self, *a, **k: (costs, bks)
 
 
+def install_proposer(llm, kind: str, prompts: list[list[int]], replay: list[list[int]] | None = None,
+                     seed: int = 0) -> None:
+    """Replace the engine's n-gram guesses (on rank 0, where the proposer runs), as the reference's bench.py does for
+    its worst case (--spec-proposer random, bench.py:143-146):
+      random  uniformly random token ids: almost never accepted, so every decode step verifies k guesses and
+              keeps only the model's own token;
+      replay  the tokens a plain greedy run produced for the same prompt (`replay`), i.e. the guesses a perfect
+              proposer would make: accepted until the first bf16 near-tie between the two runs' batch shapes.
+    Either way the speculative path (guesses shipped to every rank, verify, accept) runs on every decode step,
+    which n-gram lookups on a random-init model (whose output does not repeat itself) rarely reach."""
+    import random
+    if kind == "ngram":
+        return
+    assert llm.proposer is not None, "proposer replacement needs speculative_method='ngram'"
+    if kind == "random":
+        rng = random.Random(seed)
+        vocab = llm.config.hf_config.vocab_size
+        llm.proposer.propose = lambda seq, k: [rng.randrange(vocab) for _ in range(max(k, 0))]
+        return
+    assert kind == "replay" and replay is not None
+    by_prompt = {tuple(p): r for p, r in zip(prompts, replay)}
+
+    def propose(seq, k):
+        done = seq.num_completion_tokens
+        future = by_prompt.get(tuple(seq.prompt_token_ids), [])
+        return list(future[done:done + max(k, 0)])
+    llm.proposer.propose = propose
+
+
 def run_arm(arm: str, variant: str, prompts: list[list[int]], max_tokens: int, model_path: str, tp: int = 1,
             step_costs_file: str | None = None, save_step_costs: str | None = None, weight_seed: int = 0,
-            **engine_overrides) -> dict:
+            proposer: str = "ngram", replay: list[list[int]] | None = None, **engine_overrides) -> dict:
     """One engine run in this process: build LLM(model_path, ...) with the arm's attention, generate greedily
     (ignore_eos, exactly max_tokens per request) and return tokens, timing and speculative-decoding counters."""
     assert arm in ARMS, arm
@@ -249,6 +286,7 @@ def run_arm(arm: str, variant: str, prompts: list[list[int]], max_tokens: int, m
     t0 = time.perf_counter()
     llm = LLM(model_path, **kwargs)
     init_s = time.perf_counter() - t0
+    install_proposer(llm, proposer, prompts, replay)
     if save_step_costs and llm.step_costs is not None:
         with open(save_step_costs, "w") as f:
             json.dump({"costs": llm.step_costs, "buckets": llm.step_cost_buckets}, f)
@@ -261,7 +299,7 @@ def run_arm(arm: str, variant: str, prompts: list[list[int]], max_tokens: int, m
     tokens = [o["token_ids"] for o in outputs]
     n_out = sum(len(t) for t in tokens)
     result = {
-        "arm": arm, "variant": variant, "tp": tp, "tokens": tokens, "output_tokens": n_out,
+        "arm": arm, "variant": variant, "tp": tp, "proposer": proposer, "tokens": tokens, "output_tokens": n_out,
         "generate_s": gen_s, "output_tok_per_s": n_out / gen_s, "init_s": init_s,
         "num_kvcache_blocks": llm.config.num_kvcache_blocks, "mixed_steps": llm.num_mixed_steps,
         "spec": llm.get_spec_stats() if llm.spec_method else None,
@@ -292,6 +330,9 @@ def main(argv=None) -> None:
     p.add_argument("--step-costs", default=None, help="inject this dynamic-k cost table (JSON) if the file exists")
     p.add_argument("--synthetic-step-costs", action="store_true", help="write synthetic_step_costs() to --step-costs first")
     p.add_argument("--save-step-costs", default=None, help="write the table this arm measured")
+    p.add_argument("--proposer", choices=["ngram", "random", "replay"], default="ngram",
+                   help="replace the n-gram guesses (n-gram variants only), see install_proposer")
+    p.add_argument("--replay-from", default=None, help="--proposer replay: a result JSON of a plain greedy run")
     p.add_argument("--max-num-seqs", type=int, default=None)
     p.add_argument("--gpu-memory-utilization", type=float, default=None)
     p.add_argument("--out", required=True)
@@ -309,8 +350,12 @@ def main(argv=None) -> None:
     if a.gpu_memory_utilization:
         overrides["gpu_memory_utilization"] = a.gpu_memory_utilization
     prompts = config5_prompts(a.num_prompts, a.prompt_len, seed=a.seed)
+    replay = None
+    if a.replay_from:
+        with open(a.replay_from) as f:
+            replay = json.load(f)["tokens"]
     res = run_arm(a.arm, a.variant, prompts, a.max_tokens, model_path, a.tp, a.step_costs, a.save_step_costs,
-                  a.weight_seed, **overrides)
+                  a.weight_seed, a.proposer, replay, **overrides)
     res["prompts_seed"], res["num_prompts"], res["prompt_len"] = a.seed, a.num_prompts, a.prompt_len
     with open(a.out, "w") as f:
         json.dump(res, f)

@@ -1,0 +1,74 @@
+"""End to end with tensor parallelism (needs 2+ GPUs; skipped on one): greedy speculative decoding of a random-init
+Qwen3-8B at TP 2 (and 4 / 8 when that many GPUs are visible) under the reference's own engine, which refuses
+speculative decoding with TP > 1 (config.py:39-41) until nvattn.nanovllm_dropin.install_tp_speculative ships each
+step's guesses to the worker ranks and verifies on rank 0.  Both arms get that plumbing; the nvattn arm also gets
+the whole drop-in (attention, fused prologue, guesses verified from per-rank (max, index) keys instead of the
+full-vocabulary logits gather).
+
+The guesses replay a plain greedy run of the same arm (a perfect proposer, install_proposer 'replay'), so every
+decode step is a k = 4 verify step with its guesses on every rank; n-gram lookups rarely fire on random weights.
+Checks: every token within 0.5 of the float32 referee's top-1 (tests/e2e_referee.py, on one GPU), the guesses
+accepted at >= 85% in both arms, a clean device error word."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(REPO, "nano-vllm-spec-decode_b200")
+sys.path.insert(0, PKG)
+
+TOL, MIN_ACCEPTANCE = 0.5, 0.85
+NUM_PROMPTS, PROMPT_LEN, MAX_TOKENS = 8, 1024, 32
+
+
+def _run(cmd, timeout):
+    env = dict(os.environ, PYTHONPATH=PKG + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    r = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=timeout)
+    assert r.returncode == 0, f"{' '.join(cmd)} failed:\n{r.stdout[-3000:]}\n{r.stderr[-6000:]}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_tp_speculative_end_to_end(tmp_path, tp):
+    import torch
+    if torch.cuda.device_count() < tp:
+        pytest.skip(f"needs {tp} GPUs")
+    if not os.path.isdir(os.path.join(REPO, "baseline", "_ref", "nanovllm")):
+        pytest.skip("the reference is not installed under baseline/_ref")
+    from nvattn.e2e import write_model_dir, config5_prompts
+    model_dir = write_model_dir(str(tmp_path / "qwen3_8b_random"))
+    common = ["--model-dir", model_dir, "--tp", str(tp), "--num-prompts", str(NUM_PROMPTS), "--prompt-len",
+              str(PROMPT_LEN), "--max-tokens", str(MAX_TOKENS), "--max-num-seqs", "16"]
+    results = {}
+    for arm in ("reference", "nvattn+all"):
+        plain = tmp_path / f"{arm}_plain.json"
+        _run([sys.executable, "-m", "nvattn.e2e", "--arm", arm, "--variant", "graph", "--out", str(plain)] + common,
+             1200)
+        spec = tmp_path / f"{arm}_spec.json"
+        _run([sys.executable, "-m", "nvattn.e2e", "--arm", arm, "--variant", "spec_ngram_graph", "--proposer",
+              "replay", "--replay-from", str(plain), "--out", str(spec)] + common, 1200)
+        results[f"{arm}/plain"] = json.loads(plain.read_text())
+        results[f"{arm}/spec"] = json.loads(spec.read_text())
+    prompts = config5_prompts(NUM_PROMPTS, PROMPT_LEN)
+    (tmp_path / "runs.json").write_text(json.dumps({"prompts": prompts,
+                                                    "runs": {k: v["tokens"] for k, v in results.items()}}))
+    _run([sys.executable, os.path.join(REPO, "tests", "e2e_referee.py"), "--model-dir", model_dir,
+          "--inp", str(tmp_path / "runs.json"), "--out", str(tmp_path / "gaps.json")], 1200)
+    gaps = json.loads((tmp_path / "gaps.json").read_text())
+    report = {}
+    for name, r in results.items():
+        flat = [g for seq in gaps[name] for g in seq]
+        s = r["spec"] or {}
+        rate = s.get("num_accepted", 0) / max(s.get("num_accepted", 0) + s.get("num_rejected", 0), 1)
+        report[name] = dict(worst_gap=max(flat), tok_per_s=round(r["output_tok_per_s"], 1),
+                            k_steps=s.get("k_steps"), acceptance=round(rate, 3), device_error=r.get("device_error"))
+    print(json.dumps({"tp": tp, "runs": report}, indent=1))
+    for name, r in report.items():
+        assert r["worst_gap"] <= TOL, f"{name}: a token {r['worst_gap']:.3f} below the referee's top-1"
+        if name.endswith("/spec"):
+            assert results[name]["spec"]["num_drafts"] > 0 and r["acceptance"] >= MIN_ACCEPTANCE, (name, r)
+        if name.startswith("nvattn"):
+            assert r["device_error"] == 0, (name, r)
