@@ -290,6 +290,14 @@ def run_arm(arm: str, variant: str, prompts: list[list[int]], max_tokens: int, m
     if save_step_costs and llm.step_costs is not None:
         with open(save_step_costs, "w") as f:
             json.dump({"costs": llm.step_costs, "buckets": llm.step_cost_buckets}, f)
+    # Warm-up of the reference's own bench.py (bench.py:248-253): first calls with new shapes are slow (torch.compile
+    # of the sampler and norms, kernel setup), so one request, then four of 64-256 tokens, 32 new tokens each; their
+    # tokens share no prefix-cache block with the measured prompts.  Counters are reset after it.
+    warm = [[100 + i % (3 + j) for i in range(64 * (j + 1))] for j in range(4)]
+    for batch in (warm[:1], warm):
+        llm.generate(batch, SamplingParams(temperature=0, max_tokens=32, ignore_eos=True), use_tqdm=False)
+    llm.reset_spec_stats()
+    llm.num_mixed_steps = 0
     sp = SamplingParams(temperature=0, max_tokens=max_tokens, ignore_eos=True)
     torch.cuda.synchronize()
     t0 = time.perf_counter()

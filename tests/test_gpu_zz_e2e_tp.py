@@ -5,10 +5,15 @@ step's guesses to the worker ranks and verifies on rank 0.  Both arms get that p
 the whole drop-in (attention, fused prologue, guesses verified from per-rank (max, index) keys instead of the
 full-vocabulary logits gather).
 
-The guesses replay a plain greedy run of the same arm (a perfect proposer, install_proposer 'replay'), so every
-decode step is a k = 4 verify step with its guesses on every rank; n-gram lookups rarely fire on random weights.
-Checks: every token within 0.5 of the float32 referee's top-1 (tests/e2e_referee.py, on one GPU), the guesses
-accepted at >= 85% in both arms, a clean device error word."""
+The guesses replay a plain greedy run of the nvattn arm (a perfect proposer for it, install_proposer 'replay'), so
+every decode step is a k = 4 verify step with its guesses on every rank; n-gram lookups rarely fire on random
+weights.
+Checks: every token within 0.5 of the float32 referee's top-1 (tests/e2e_referee.py, on one GPU), guesses checked
+on every decode step, and a clean device error word.  With this package's attention the replayed guesses are
+accepted at >= 85% (its decode and verify kernels compute each query row with the same arithmetic, so a verify step
+reproduces the plain run's argmaxes); the reference's flash-attn rounds its verify calls differently from its decode
+calls (another split of the keys), so its run departs from the replayed one at the first bf16 near-tie and the later
+guesses of that request are rejected: its acceptance is reported, not checked."""
 import json
 import os
 import subprocess
@@ -43,14 +48,14 @@ def test_tp_speculative_end_to_end(tmp_path, tp):
     common = ["--model-dir", model_dir, "--tp", str(tp), "--num-prompts", str(NUM_PROMPTS), "--prompt-len",
               str(PROMPT_LEN), "--max-tokens", str(MAX_TOKENS), "--max-num-seqs", "16"]
     results = {}
+    plain = tmp_path / "plain.json"     # the guesses of both arms replay this plain greedy run
+    _run([sys.executable, "-m", "nvattn.e2e", "--arm", "nvattn+all", "--variant", "graph", "--out", str(plain)] + common,
+         1200)
+    results["nvattn+all/plain"] = json.loads(plain.read_text())
     for arm in ("reference", "nvattn+all"):
-        plain = tmp_path / f"{arm}_plain.json"
-        _run([sys.executable, "-m", "nvattn.e2e", "--arm", arm, "--variant", "graph", "--out", str(plain)] + common,
-             1200)
         spec = tmp_path / f"{arm}_spec.json"
         _run([sys.executable, "-m", "nvattn.e2e", "--arm", arm, "--variant", "spec_ngram_graph", "--proposer",
               "replay", "--replay-from", str(plain), "--out", str(spec)] + common, 1200)
-        results[f"{arm}/plain"] = json.loads(plain.read_text())
         results[f"{arm}/spec"] = json.loads(spec.read_text())
     prompts = config5_prompts(NUM_PROMPTS, PROMPT_LEN)
     (tmp_path / "runs.json").write_text(json.dumps({"prompts": prompts,
@@ -69,6 +74,8 @@ def test_tp_speculative_end_to_end(tmp_path, tp):
     for name, r in report.items():
         assert r["worst_gap"] <= TOL, f"{name}: a token {r['worst_gap']:.3f} below the referee's top-1"
         if name.endswith("/spec"):
-            assert results[name]["spec"]["num_drafts"] > 0 and r["acceptance"] >= MIN_ACCEPTANCE, (name, r)
+            assert results[name]["spec"]["num_drafts"] > 0, (name, r)
+        if name == "nvattn+all/spec":
+            assert r["acceptance"] >= MIN_ACCEPTANCE, (name, r)
         if name.startswith("nvattn"):
             assert r["device_error"] == 0, (name, r)
