@@ -36,27 +36,28 @@ def _run(cmd, timeout):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("tp", [2, 4, 8])
-def test_tp_speculative_end_to_end(tmp_path, tp):
+def test_tp_speculative_end_to_end(tmp_path):
     import torch
-    if torch.cuda.device_count() < tp:
-        pytest.skip(f"needs {tp} GPUs")
+    tps = [tp for tp in (2, 4, 8) if tp <= torch.cuda.device_count()]
+    if not tps:
+        pytest.skip("needs 2 or more GPUs")
     if not os.path.isdir(os.path.join(REPO, "baseline", "_ref", "nanovllm")):
         pytest.skip("the reference is not installed under baseline/_ref")
     from nvattn.e2e import write_model_dir, config5_prompts
     model_dir = write_model_dir(str(tmp_path / "qwen3_8b_random"))
-    common = ["--model-dir", model_dir, "--tp", str(tp), "--num-prompts", str(NUM_PROMPTS), "--prompt-len",
-              str(PROMPT_LEN), "--max-tokens", str(MAX_TOKENS), "--max-num-seqs", "16"]
     results = {}
-    plain = tmp_path / "plain.json"     # the guesses of both arms replay this plain greedy run
-    _run([sys.executable, "-m", "nvattn.e2e", "--arm", "nvattn+all", "--variant", "graph", "--out", str(plain)] + common,
-         1200)
-    results["nvattn+all/plain"] = json.loads(plain.read_text())
-    for arm in ("reference", "nvattn+all"):
-        spec = tmp_path / f"{arm}_spec.json"
-        _run([sys.executable, "-m", "nvattn.e2e", "--arm", arm, "--variant", "spec_ngram_graph", "--proposer",
-              "replay", "--replay-from", str(plain), "--out", str(spec)] + common, 1200)
-        results[f"{arm}/spec"] = json.loads(spec.read_text())
+    for tp in tps:
+        common = ["--model-dir", model_dir, "--tp", str(tp), "--num-prompts", str(NUM_PROMPTS), "--prompt-len",
+                  str(PROMPT_LEN), "--max-tokens", str(MAX_TOKENS), "--max-num-seqs", "16"]
+        plain = tmp_path / f"plain_tp{tp}.json"     # the guesses of both arms replay this plain greedy run
+        _run([sys.executable, "-m", "nvattn.e2e", "--arm", "nvattn+all", "--variant", "graph", "--out", str(plain)]
+             + common, 1200)
+        results[f"tp{tp}/nvattn+all/plain"] = json.loads(plain.read_text())
+        for arm in ("reference", "nvattn+all"):
+            spec = tmp_path / f"{arm}_spec_tp{tp}.json"
+            _run([sys.executable, "-m", "nvattn.e2e", "--arm", arm, "--variant", "spec_ngram_graph", "--proposer",
+                  "replay", "--replay-from", str(plain), "--out", str(spec)] + common, 1200)
+            results[f"tp{tp}/{arm}/spec"] = json.loads(spec.read_text())
     prompts = config5_prompts(NUM_PROMPTS, PROMPT_LEN)
     (tmp_path / "runs.json").write_text(json.dumps({"prompts": prompts,
                                                     "runs": {k: v["tokens"] for k, v in results.items()}}))
@@ -70,12 +71,12 @@ def test_tp_speculative_end_to_end(tmp_path, tp):
         rate = s.get("num_accepted", 0) / max(s.get("num_accepted", 0) + s.get("num_rejected", 0), 1)
         report[name] = dict(worst_gap=max(flat), tok_per_s=round(r["output_tok_per_s"], 1),
                             k_steps=s.get("k_steps"), acceptance=round(rate, 3), device_error=r.get("device_error"))
-    print(json.dumps({"tp": tp, "runs": report}, indent=1))
+    print(json.dumps(report, indent=1))
     for name, r in report.items():
         assert r["worst_gap"] <= TOL, f"{name}: a token {r['worst_gap']:.3f} below the referee's top-1"
         if name.endswith("/spec"):
             assert results[name]["spec"]["num_drafts"] > 0, (name, r)
-        if name == "nvattn+all/spec":
+        if name.endswith("nvattn+all/spec"):
             assert r["acceptance"] >= MIN_ACCEPTANCE, (name, r)
-        if name.startswith("nvattn"):
+        if "nvattn" in name:
             assert r["device_error"] == 0, (name, r)
