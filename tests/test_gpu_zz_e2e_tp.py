@@ -9,11 +9,14 @@ The guesses replay a plain greedy run of the nvattn arm (a perfect proposer for 
 every decode step is a k = 4 verify step with its guesses on every rank; n-gram lookups rarely fire on random
 weights.
 Checks: every token within 0.5 of the float32 referee's top-1 (tests/e2e_referee.py, on one GPU), guesses checked
-on every decode step, and a clean device error word.  With this package's attention the replayed guesses are
-accepted at >= 85% (its decode and verify kernels compute each query row with the same arithmetic, so a verify step
-reproduces the plain run's argmaxes); the reference's flash-attn rounds its verify calls differently from its decode
-calls (another split of the keys), so its run departs from the replayed one at the first bf16 near-tie and the later
-guesses of that request are rejected: its acceptance is reported, not checked."""
+on every decode step, and a clean device error word.  At TP 2 the replayed guesses are accepted at >= 85% with this
+package's attention: its decode and verify kernels compute each query row with the same arithmetic, and the
+all-reduce of two partial sums does not depend on the order NCCL adds them in, so a verify step reproduces the plain
+run's argmaxes.  The reference's flash-attn rounds its verify calls differently from its decode calls (another split
+of the keys), and from TP 4 on NCCL adds the ranks' partial sums in an order that depends on the message size (a
+verify step all-reduces 1 + k times more rows), so in those runs the verify pass departs from the replayed one at the
+first bf16 near-tie and the request's later guesses are rejected: their acceptance is reported, not checked.
+NVA_E2E_TPS (e.g. "8") limits the tensor-parallel sizes run."""
 import json
 import os
 import subprocess
@@ -38,7 +41,8 @@ def _run(cmd, timeout):
 @pytest.mark.gpu
 def test_tp_speculative_end_to_end(tmp_path):
     import torch
-    tps = [tp for tp in (2, 4, 8) if tp <= torch.cuda.device_count()]
+    wanted = [int(x) for x in os.environ.get("NVA_E2E_TPS", "2,4,8").split(",")]
+    tps = [tp for tp in wanted if tp <= torch.cuda.device_count()]
     if not tps:
         pytest.skip("needs 2 or more GPUs")
     if not os.path.isdir(os.path.join(REPO, "baseline", "_ref", "nanovllm")):
@@ -76,7 +80,7 @@ def test_tp_speculative_end_to_end(tmp_path):
         assert r["worst_gap"] <= TOL, f"{name}: a token {r['worst_gap']:.3f} below the referee's top-1"
         if name.endswith("/spec"):
             assert results[name]["spec"]["num_drafts"] > 0, (name, r)
-        if name.endswith("nvattn+all/spec"):
+        if name == "tp2/nvattn+all/spec":
             assert r["acceptance"] >= MIN_ACCEPTANCE, (name, r)
         if "nvattn" in name:
             assert r["device_error"] == 0, (name, r)
