@@ -538,11 +538,12 @@ def fa2_rows(world, rank, args, flush, b, q4, lens, H, KVH):
     return rows
 
 
-def cpu_sample(seed, nseq):
-    """The first nseq sequences of the config-2 batch, generated on the CPU (same lengths as the GPU run)."""
+def cpu_sample(seed, nseq, total=64):
+    """The first nseq sequences of the config-2 batch of `total` sequences (the GPU arm's lengths at N = total / 64),
+    generated on the CPU."""
     from nvattn.workloads import paged_decode_batch
     g = torch.Generator().manual_seed(seed)
-    lens = torch.randint(512, 4097, (64,), generator=g).tolist()[:nseq]
+    lens = torch.randint(512, 4097, (total,), generator=g).tolist()[:nseq]
     nblk = sum((L + 255) // 256 for L in lens)
     b = paged_decode_batch(lens, 1, 32, 8, 128, nblk, 0.5, seed + 1, device="cpu")
     return b, lens
@@ -574,28 +575,32 @@ def cpu_baseline(seed, budget_s=10.0):
 
 
 def run_reference(args, world, rank):
-    """Reference arm: the reference semantics on the host cores (FP32 torch oracle), same metric and config."""
+    """Reference arm: the reference semantics on the host cores (FP32 torch oracle) with every host thread, on this
+    arm's whole config-2 job: all 64 x N sequences and all 32 q / 8 kv heads per step (the GPU arm splits the heads
+    over its N ranks).  Rank 0 alone runs it."""
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    b, lens = cpu_sample(args.seed, 2)
+    nseq = 64 * world
+    b, lens = cpu_sample(args.seed, nseq, total=nseq)
     by = attn_bytes(lens, 1, 32, 8)
     import oracle
     q = b.q.view(len(lens), 1, 32, 128)
-    for _ in range(max(1, min(args.warmup, 3))):
+    warmup = 1 if world > 1 else max(1, min(args.warmup, 3))
+    for _ in range(warmup):
         oracle.paged_attention_ref(q, b.k_cache, b.v_cache, b.context_lens, b.block_tables, b.scale)
-    steps = max(1, min(args.steps, 20))
+    steps = max(1, min(args.steps, 20 if world == 1 else 10))
     t0 = time.perf_counter()
     for _ in range(steps):
         oracle.paged_attention_ref(q, b.k_cache, b.v_cache, b.context_lens, b.block_tables, b.scale)
     dt = (time.perf_counter() - t0) / steps
     value = by / dt / 1e9
-    sample = f"first 2 of the 64 config-2 sequences ({sum(lens)} tokens) per step, {steps} steps"
+    sample = f"the whole job: all {nseq} config-2 sequences ({sum(lens)} tokens), all heads, per step; {steps} steps"
     line = {"impl": "reference", "metric": "decode attention HBM GB/s (BASELINE config 2: Qwen3-8B paged decode)",
-            "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": warmup,
             "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded; BASELINE config 2 shapes)",
-            "config": {"workload": "paged decode attention, BASELINE config 2 (sampled)", "global_batch": 2,
+            "config": {"workload": "paged decode attention, BASELINE config 2", "global_batch": nseq,
                        "parallelism": "host cores"},
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
                              "kind": "port", "sample": sample},
