@@ -132,7 +132,7 @@ NVA_API int nva_greedy_accept(const void* target_ids, int64_t target_row_stride,
  *   k_cache / v_cache rows (the nva_store_kvcache layout) at slot = slot_mapping[t] of k' and of v, when
  *   slot_mapping != NULL; slot -1 is skipped, slots past num_slots are skipped and set bit 1 of the error word.
  * rope: x1 = dims [0, D/2), x2 = dims [D/2, D): (x1 cos - x2 sin, x2 cos + x1 sin) in float32, rounded to bf16.
- * head_dim 128.  Positions outside [0, max_position) are clamped.
+ * head_dim 128, num_heads + 2 * num_kv_heads <= 64.  Positions outside [0, max_position) are clamped.
  */
 NVA_API int nva_qk_norm_rope_store(const void* qkv, int64_t qkv_row_stride, int32_t num_tokens, int32_t num_heads,
                                    int32_t num_kv_heads, int32_t head_dim, const int64_t* positions,

@@ -358,6 +358,7 @@ NVA_API int nva_qk_norm_rope_store(const void* qkv, int64_t qkv_row_stride, int3
   if (num_tokens < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_position <= 0 || num_slots < 0)
     return NVA_ERR_INVALID_ARGUMENT;
   if (head_dim != nva::kHeadDim) return NVA_ERR_UNSUPPORTED;
+  if (num_heads + 2 * num_kv_heads > 64) return NVA_ERR_UNSUPPORTED;   // one block of 8 warps x 8 heads per token
   if (num_tokens == 0) return NVA_OK;
   if (qkv == nullptr || positions == nullptr || cos_sin == nullptr || q_norm_weight == nullptr ||
       k_norm_weight == nullptr || q_out == nullptr)

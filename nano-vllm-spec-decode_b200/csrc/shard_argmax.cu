@@ -11,6 +11,7 @@
 // shard_accept: merges the keys of all shards into the target ids and applies the greedy accept rule
 // (sampler.py:79-82) in the same thread: one thread per sequence.
 #include <algorithm>
+#include <type_traits>
 
 #include "nva_kernels.h"
 
@@ -44,6 +45,7 @@ shard_argmax_kernel(const T* __restrict__ logits, int64_t row_stride, int32_t vo
   const T* p = logits + static_cast<int64_t>(row) * row_stride;
   float best = -__int_as_float(0x7F800000);    // -inf
   int best_i = -1;
+  int best_v = -1;   // bf16: the vector holding the first occurrence of `best`
   if constexpr (VEC > 1) {
     // chunk and row starts are multiples of VEC elements (16 bytes): whole vectors, four loads in flight per
     // thread (its elements stay in increasing index order), then the row's ragged end
@@ -56,17 +58,46 @@ shard_argmax_kernel(const T* __restrict__ logits, int64_t row_stride, int32_t vo
         const int v = v0 + u * kArgmaxThreads;
         if (v < nvec) raw[u] = __ldg(reinterpret_cast<const uint4*>(p + c0 + v * VEC));
       }
+      if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+        // bf16: per 16-byte vector, its maximum with packed NaN-propagating max instructions, and the vector that
+        // first reached the running maximum; the element's position inside that vector is found once at the end
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int v = v0 + u * kArgmaxThreads;
-        if (v >= nvec) break;
-        const T* e = reinterpret_cast<const T*>(&raw[u]);
+        for (int u = 0; u < kUnroll; ++u) {
+          const int v = v0 + u * kArgmaxThreads;
+          if (v < nvec) {
+            const __nv_bfloat162* e2 = reinterpret_cast<const __nv_bfloat162*>(&raw[u]);
+            const __nv_bfloat162 m2 = __hmax2_nan(__hmax2_nan(e2[0], e2[1]), __hmax2_nan(e2[2], e2[3]));
+            const float vm = __bfloat162float(__hmax_nan(__low2bfloat16(m2), __high2bfloat16(m2)));
+            const bool take = best_v < 0 || beats(vm, best);
+            best = take ? vm : best;
+            best_v = take ? v : best_v;
+          }
+        }
+      } else {
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          const float x = widen(e[j]);
-          if (best_i < 0 || beats(x, best)) { best = x; best_i = c0 + v * VEC + j; }
+        for (int u = 0; u < kUnroll; ++u) {
+          const int v = v0 + u * kArgmaxThreads;
+          if (v >= nvec) break;
+          const T* e = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            const float x = widen(e[j]);
+            if (best_i < 0 || beats(x, best)) { best = x; best_i = c0 + v * VEC + j; }
+          }
         }
       }
+    }
+    if (best_v >= 0) {   // bf16: the first element of the best vector equal to its maximum (a NaN when it is NaN)
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p + c0 + best_v * VEC));
+      const T* e = reinterpret_cast<const T*>(&raw);
+      const bool want_nan = best != best;
+      int j = VEC - 1;
+#pragma unroll
+      for (int q = VEC - 1; q >= 0; --q) {
+        const float x = widen(e[q]);
+        j = (want_nan ? x != x : x == best) ? q : j;
+      }
+      best_i = c0 + best_v * VEC + j;
     }
     for (int i = c0 + nvec * VEC + threadIdx.x; i < c1; i += kArgmaxThreads) {
       const float x = widen(p[i]);
