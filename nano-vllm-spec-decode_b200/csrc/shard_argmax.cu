@@ -49,7 +49,7 @@ shard_argmax_kernel(const T* __restrict__ logits, int64_t row_stride, int32_t vo
   if constexpr (VEC > 1) {
     // chunk and row starts are multiples of VEC elements (16 bytes): whole vectors, four loads in flight per
     // thread (its elements stay in increasing index order), then the row's ragged end
-    constexpr int kUnroll = 4;
+    constexpr int kUnroll = 8;
     const int nvec = (c1 - c0) / VEC;
     for (int v0 = threadIdx.x; v0 < nvec; v0 += kUnroll * kArgmaxThreads) {
       uint4 raw[kUnroll];
