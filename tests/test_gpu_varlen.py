@@ -223,3 +223,51 @@ def test_attention_module_decode_graph(cuda):
     ref = oracle.paged_attention_ref(b.q.cpu().view(3, n, H, 128), b.k_cache.cpu(), b.v_cache.cpu(),
                                      b.context_lens.cpu(), b.block_tables.cpu(), b.scale)
     assert_attn_close(out.view(3, n, H, 128), ref, "graph decode")
+
+
+def test_workspace_reserved_before_capture_and_never_grown_in_one(cuda):
+    """nvattn.ops keeps one attention workspace per device.  A call that needs a bigger one while a CUDA graph is
+    being captured raises instead of allocating inside the capture (which would give the graph a private
+    allocation and record a zero-fill into every replay); after ops.reserve_workspace(max_num_seqs,
+    max_num_batched_tokens, ...) -- what the nano-vllm drop-in does when the KV cache is allocated -- a larger call
+    captures without allocating and replays equal to the eager call."""
+    from nvattn import ops
+    from nvattn.workloads import mixed_config
+    saved = dict(ops._WORKSPACES)
+    ops._WORKSPACES.clear()
+    try:
+        small = batch([1, 40], [100, 300], seed=13)
+        run_varlen(small)                       # sizes a workspace for 2 sequences
+        big = mixed_config(seed=0, device="cuda")   # 259 sequences: needs more
+        out = torch.empty_like(big.q)
+
+        def call():
+            ops.flash_attn_varlen_func(big.q, big.k_cache, big.v_cache, max_seqlen_q=big.max_seqlen_q,
+                                       cu_seqlens_q=big.cu_seqlens_q, max_seqlen_k=big.max_seqlen_k,
+                                       cu_seqlens_k=big.cu_seqlens_k, softmax_scale=big.scale, causal=True,
+                                       block_table=big.block_tables, out=out)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with pytest.raises(RuntimeError, match="reserve_workspace"):
+            with torch.cuda.graph(g):
+                call()
+        del g
+        ops.reserve_workspace(512, 16384, 32, 8)
+        ws = ops._WORKSPACES[torch.cuda.current_device()]
+        call()
+        torch.cuda.synchronize()
+        ref = out.clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2):
+            call()
+        out.fill_(float("nan"))
+        g2.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+        assert ops._WORKSPACES[torch.cuda.current_device()] is ws     # nothing was allocated or grown
+        del g2
+    finally:
+        ops._WORKSPACES.clear()
+        ops._WORKSPACES.update(saved)
