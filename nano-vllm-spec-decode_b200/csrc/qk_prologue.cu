@@ -27,7 +27,7 @@ __device__ __forceinline__ float2 bf16r2(float2 v) {
 }
 
 // One block per token, one warp per group of 8 heads (q heads, then k heads, then v heads).
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
 qk_prologue_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t qkv_stride, int32_t H, int32_t KVH,
                    const int64_t* __restrict__ positions, const float* __restrict__ cos_sin, int32_t max_pos,
                    const __nv_bfloat16* __restrict__ q_w, const __nv_bfloat16* __restrict__ k_w, float eps,
