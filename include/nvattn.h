@@ -64,7 +64,9 @@ NVA_API int nva_store_kvcache(const void* key, int64_t key_row_stride, const voi
  *     query i of sequence b attends to cache positions [0, context_lens[b] - q_per_seq + i].
  * context_lens include the q_per_seq new tokens (already stored by nva_store_kvcache).  A sequence with
  * context length 0 (batch padding) reads nothing and gets a zero output.  q_per_seq * (H / KVH) <= 48.
- * Requires head_dim 128, bf16, block_size a multiple of 128.  workspace >= nva_paged_decode_workspace_bytes().
+ * Requires head_dim 128, bf16, block_size a multiple of 128, softmax_scale positive and finite (else
+ * NVA_ERR_INVALID_ARGUMENT; also for nva_varlen_attention and nva_paged_decode_noalloc).
+ * workspace >= nva_paged_decode_workspace_bytes().
  * Workspace contract: zero-fill it once before its first use (cudaMemset); every call leaves its first 256-byte
  * aligned block of merge tickets at zero again, so the same workspace serves every later call in stream order (also
  * nva_varlen_attention calls, and captured CUDA graphs).  Calls that may overlap on one device (different streams)

@@ -75,6 +75,9 @@ int sm_count() {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// The attention kernels take row maxima of unscaled scores and scale them afterwards: the scale must be positive
+// (and finite); NaN fails the comparison.
+bool valid_scale(float s) { return s > 0.f && s < 3.0e38f; }
 
 int check_cache(const void* k_cache, const void* v_cache, int32_t num_blocks, int32_t block_size, int32_t kvh) {
   if (k_cache == nullptr || v_cache == nullptr || num_blocks <= 0 || block_size <= 0 || kvh <= 0)
@@ -141,6 +144,7 @@ NVA_API int nva_paged_decode(const void* q, int64_t q_row_stride, const void* k_
                              void* stream) {
   if (num_seqs < 0 || q_per_seq < 1 || num_heads <= 0 || num_kv_heads <= 0) return NVA_ERR_INVALID_ARGUMENT;
   if (num_heads % num_kv_heads != 0) return NVA_ERR_INVALID_ARGUMENT;
+  if (!valid_scale(softmax_scale)) return NVA_ERR_INVALID_ARGUMENT;
   if (head_dim != nva::kHeadDim) return NVA_ERR_UNSUPPORTED;
   if (num_seqs == 0) return NVA_OK;
   if (num_seqs > nva::kMaxDecodeSeqs) return NVA_ERR_UNSUPPORTED;
@@ -224,6 +228,7 @@ NVA_API int nva_varlen_attention(const void* q, int64_t q_row_stride, const void
   if (num_seqs < 0 || total_q < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_seqlen_q < 0 || max_seqlen_k < 0)
     return NVA_ERR_INVALID_ARGUMENT;
   if (num_heads % num_kv_heads != 0) return NVA_ERR_INVALID_ARGUMENT;
+  if (!valid_scale(softmax_scale)) return NVA_ERR_INVALID_ARGUMENT;
   if (head_dim != nva::kHeadDim) return NVA_ERR_UNSUPPORTED;
   if (num_seqs == 0 || total_q == 0) return NVA_OK;
   if (num_seqs > nva::kMaxDecodeSeqs) return NVA_ERR_UNSUPPORTED;

@@ -46,14 +46,16 @@ constexpr uint32_t kFull = 0xffffffffu;
 // warps, so an entry is never rewritten before the softmax warps have read it.
 constexpr int kInfoRing = 8;
 
-constexpr int kMergePieces = 16;
+constexpr int kMergePieces = 16;   // pieces of a cut segment merged through the shared weight table
 constexpr int kTicketStride = 4;   // merge tickets per CTA: one per softmax warpgroup (at most 3)
 // Row maxima move only when a score passes them by more than this (log2 units): until then P <= 2^8, exact enough in
 // bf16 and in the FP32 sums.
-constexpr float kRescaleLog2 = 8.0f;   // pieces of a cut segment merged through the shared weight table
+constexpr float kRescaleLog2 = 8.0f;
+constexpr float kRescaleSum = 256.0f;   // 2^kRescaleLog2: a thread's weights adding up to this ask for the exact maxima
 
-template <int NP>
+template <int NP, bool Spec = false>
 struct Cfg {
+  static_assert(!Spec || NP == 48, "the speculative-weights variant is a 48-row instantiation");
   // softmax warpgroups (row shares): two at 32/48 rows.  Three at 48 rows measured 69 vs 72 us on verify k = 8 but
   // 216 vs 210 us on config 4's mixed step (short segments leave two groups idle; 128 registers a thread spill)
   static constexpr int kWG = NP >= 32 ? 2 : 1;
@@ -67,6 +69,13 @@ struct Cfg {
   // P^T / O buffers: two at 32/48 rows, so a tile's P is handed to the tensor pipe before the previous tile's O is
   // folded (verify k = 8 69.6 -> 65.5 us, mixed step 186 -> 181 us); one at 16 rows, where HBM sets the pace
   static constexpr int kPBuf = NP >= 32 ? 2 : 1;
+  // Spec (the 48-row variant for fixed-length verify batches): the O accumulator stays in TMEM (PV(j) adds onto its
+  // segment's O; two O buffers, by segment parity), so the softmax warps touch O only at a segment's end and when a
+  // tile moves some row maxima (scaled by alpha before PV(j) adds on); and the weights are taken before the rescale
+  // vote, against the running maxima, their per-thread sum deciding the vote.  Otherwise each PV(j) is written fresh
+  // and folded into registers, and the vote compares scores with the maxima first.
+  static constexpr bool kOAcc = Spec;
+  static constexpr bool kSpec = Spec;
   static constexpr int kK = 0;                                   // K ring
   static constexpr int kV = kKStages * kTileBytes;               // V ring
   static constexpr int kQ = (kKStages + kVStages) * kTileBytes;  // Q buffers, NP * 256 bytes each
@@ -75,8 +84,9 @@ struct Cfg {
   static constexpr int kBars = kP + kPBuf * NP * 256;            // kBarCount x u64
   static constexpr int kInfo = kBars + (kBarCount * 8 + 15) / 16 * 16;   // kInfoRing x 2 x int4
   static constexpr int kRed = kInfo + kInfoRing * 32;            // [2][4][NP] column maxima per warp
-  static constexpr int kM = kRed + 2 * 4 * NP * 4;               // [NP] running max
-  static constexpr int kAlpha = kM + NP * 4;                     // [2][NP] rescale factors
+  static constexpr int kM = kRed + 2 * 4 * NP * 4;               // [NP] running max (log2 units)
+  static constexpr int kNegM = kM + NP * 4;                      // (kSpec) [NP] its negation, 0 for -inf
+  static constexpr int kAlpha = kNegM + (kSpec ? NP * 4 : 0);    // [2][NP] rescale factors
   static constexpr int kLred = kAlpha + 2 * NP * 4;              // [4][NP] column sums per warp
   static constexpr int kRowOut = kLred + 4 * NP * 4;             // [NP] per-row output offset (int64)
   static constexpr int kRowInv = kRowOut + NP * 8;               // [NP] per-row 1 / sum
@@ -90,9 +100,10 @@ struct Cfg {
   static constexpr int kBytes = kEnd + 1024;                     // + slack for 1024-byte alignment
 };
 
-// S is double buffered by tile parity (S(j) in buffer j & 1); P and O by tile parity when Cfg::kPBuf = 2 (P(j) and
-// O(j) = P(j) V(j) in buffer j & 1), else single (buffer 0).  The barriers of P / O buffer b: pfull_bar(b),
-// ofull_bar(b) (buffer 1's come last, so one-buffer instantiations keep a 31-barrier area).
+// S is double buffered by tile parity (S(j) in buffer j & 1); P by tile parity when Cfg::kPBuf = 2 (P(j) in buffer
+// j & 1, with O in buffer (segment parity) accumulated over the segment's tiles), else single (buffer 0, O(j) =
+// P(j) V(j) written fresh).  The barriers of P buffer b: pfull_bar(b), and ofull_bar(b) (completes when the PV
+// product that read P buffer b finished); buffer 1's come last, so one-buffer instantiations keep a 31-barrier area.
 enum {
   B_KFULL = 0, B_KEMPTY = 3, B_VFULL = 6, B_VEMPTY = 9, B_SFULL = 12, B_SEMPTY = 14, B_PFULL = 16, B_OFULL = 17,
   B_QFULL = 18, B_QEMPTY = 20, B_INFO = 22,   // B_INFO + kInfoRing <= B_KSTART
@@ -479,11 +490,11 @@ __device__ __forceinline__ void merge_pieces(const DecodeParams& p, int c0, int 
   }
 }
 
-template <int NP>
-__global__ void __launch_bounds__(Cfg<NP>::kThreads, 1)
+template <int NP, bool Spec>
+__global__ void __launch_bounds__(Cfg<NP, Spec>::kThreads, 1)
 paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const DecodeParams p) {
-  using C = Cfg<NP>;
+  using C = Cfg<NP, Spec>;
   // P / O buffer of tile t and the phase parity of its barriers
   auto pbuf = [](int t) { return C::kPBuf == 2 ? (t & 1) : 0; };
   auto pphase = [](int t) { return C::kPBuf == 2 ? ((t >> 1) & 1) : (t & 1); };
@@ -493,6 +504,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   int4* info = reinterpret_cast<int4*>(smem + C::kInfo);       // [kInfoRing][2]
   float* red = reinterpret_cast<float*>(smem + C::kRed);
   float* m_s = reinterpret_cast<float*>(smem + C::kM);
+  float* negm_s = reinterpret_cast<float*>(smem + C::kNegM);
   float* alpha_s = reinterpret_cast<float*>(smem + C::kAlpha);
   float* lred = reinterpret_cast<float*>(smem + C::kLred);
   int64_t* row_out = reinterpret_cast<int64_t*>(smem + C::kRowOut);
@@ -678,21 +690,27 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     };
     issue_qk();
     issue_qk();
+    int oseg = 0;   // O buffer of the segment of tile pv (segment parity) when O accumulates in TMEM
     while (ok && pv < ntiles) {
       const int st = pv % C::kVStages;
-      const int pb = pbuf(pv);   // P / O buffer of this tile
+      const int pb = pbuf(pv);   // P buffer of this tile
       if (!mbar_wait_warp(&bars[pfull_bar(pb)], pphase(pv), abort)) break;
       if (!mbar_wait_warp(&bars[B_VFULL + st], (pv / C::kVStages) & 1, abort)) break;
-      const uint32_t idesc_pv =
-          umma_idesc_bf16(128, min(NP, mma_width(info[2 * (pv % kInfoRing) + 1].x * G)), true, true);
+      const int e = pv % kInfoRing;
+      const bool seg_first = C::kOAcc && (info[2 * e].w & 1);
+      if (seg_first && pv > 0) oseg ^= 1;
+      // O^T target and accumulate flag: the segment's accumulator (fresh at its first tile), or a fresh product
+      const uint32_t o_col = C::kOAcc ? (2 + oseg) * NP : (2 + pb) * NP;
+      const uint32_t o_acc = C::kOAcc && !seg_first ? 1u : 0u;
+      const uint32_t idesc_pv = umma_idesc_bf16(128, min(NP, mma_width(info[2 * e + 1].x * G)), true, true);
       tc_fence_after();
       if (umma_lane<NP>(lane)) {
         // A = V^T: 16 tokens per step (two 8-row groups, SBO 1024; two 64-dim slabs, LBO 16 KB) -> +2048 B;
         // B = P^T: 16 tokens per step (two 8-token core-matrix groups, LBO 128; 8-row groups, SBO 2048) -> +256 B
         constexpr uint32_t kOffV[8] = {0, 128, 256, 384, 512, 640, 768, 896};
         constexpr uint32_t kOffP[8] = {0, 16, 32, 48, 64, 80, 96, 112};
-        umma_bf16_ss_x8(tmem + (2 + pb) * NP, v_desc0 + ((st * kTileBytes) >> 4), p_desc0 + ((pb * NP * 256) >> 4),
-                        idesc_pv, 0u, kOffV, kOffP);
+        umma_bf16_ss_x8(tmem + o_col, v_desc0 + ((st * kTileBytes) >> 4), p_desc0 + ((pb * NP * 256) >> 4),
+                        idesc_pv, o_acc, kOffV, kOffP);
         umma_commit(&bars[ofull_bar(pb)]);
         umma_commit(&bars[B_VEMPTY + st]);
       }
@@ -746,6 +764,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     int R = 0, nr = 8, n = 0, L = 0, q0 = 0, seg_s0 = 0, seg_s1 = 0, seg_g = 0, seg_b = 0;
     bool alive = true;
     bool rescaled_prev = false;               // whether the previous tile moved some row maxima (alpha != 1)
+    int ob = 0;                               // O accumulator of the current segment (Cfg::kOAcc): segment parity
     // A piece of a cut segment is done (this group's rows [rb, rb + hr) written): take the group's ticket for the
     // segment; the group that brings it to the number of pieces merges those rows of all pieces and puts the
     // counter back to zero, so the counters are zero again when the launch ends (the workspace contract).  Every
@@ -775,6 +794,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       int4 inf = make_int4(0, 0, 0, 0);
       if (alive) inf = info[2 * e];
       const bool first = inf.w & 1, last = inf.w & 2;
+      if (C::kOAcc && first && jj > 0) ob ^= 1;
       if (alive && first) {
         const int4 sh = info[2 * e + 1];
         n = sh.x;
@@ -789,7 +809,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
 #pragma unroll
         for (int r = 0; r < NPH; ++r) {
           l[r] = 0.f;
-          o[r] = 0.f;
+          if constexpr (!C::kOAcc) o[r] = 0.f;   // (in TMEM, O starts fresh with the segment's first PV)
         }
       }
       const int hr = group_rows_rt(C::kWG, nr);
@@ -802,40 +822,82 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         // as the working group does, so no arrival can land in a phase that the other group has not reached.
         alive = alive && mbar_wait_warp(&bars[B_SFULL + buf], (jj >> 1) & 1, abort);
         if (alive) mbar_arrive(&bars[B_SEMPTY + buf]);
-        // (two groups: always two P / O buffers)
+        // (two groups: always two P buffers)
         if (jj >= 2) alive = alive && mbar_wait_warp(&bars[ofull_bar(pbuf(jj))], pphase(jj - 2), abort);
         if (alive) mbar_arrive(&bars[pfull_bar(pbuf(jj))]);
         if (named_bar_any(bar_id, 128, !alive)) break;
         continue;
       }
-      // ---- S tile -> masked, scaled scores.  Row maxima are lazy: scores are scaled by each row's m_s, and the
-      // exact tile maxima are taken (per-warp column maxima -> row owners) only when some score exceeds its row's
-      // m_s by more than 2^kRescaleLog2 (always at a segment's first tile); otherwise alpha = 1 and the reduction
-      // and two barriers are skipped.  P stays below 2^kRescaleLog2 either way.
+      // ---- S tile -> weights.  Row maxima are lazy: the weights P = 2^(s * scale - m) are taken against each row's
+      // running maximum m, and the exact tile maxima (per-warp column maxima -> row owners) only at a segment's
+      // first tile and when some weight could reach 2^kRescaleLog2; otherwise alpha = 1 and the reduction and two
+      // barriers are skipped.  Either way every weight stays below 2^kRescaleLog2.
+      //   kSpec (48 rows): the weights come first (packed FP32 pairs) and a thread whose weights add up to
+      //   2^kRescaleLog2 votes for the exact path, which loads the unscaled scores again (the S buffer is released
+      //   after the vote) and takes the weights against the new maxima.  Tiles that every row sees in full skip the
+      //   mask: rows past R (up to the UMMA N) hold zero scores there, from the zero-filled Q rows, and weigh nothing
+      //   (offset -128).
+      //   Otherwise: scores are masked and scaled, the vote compares them with m + 2^kRescaleLog2, and the weights
+      //   follow it.
       alive = alive && mbar_wait_warp(&bars[B_SFULL + buf], (jj >> 1) & 1, abort);
       bool need = first;
-      if (alive) {
-        tc_fence_after();
-        // query i of the segment sees tokens <= L - n + i, i.e. row r = i*G + h is visible iff r >= G*(tok-L+n)
-        const int d = tok - (L - n);
-        const int rmin = d > 0 ? d * G : 0;
-        with_rows<NP>(nr, [&](auto nr_c) {
-          constexpr int HR = group_rows<NP, decltype(nr_c)::value>();
-          tmem_ld_cols<HR>(t_lane + buf * NP + rb, s);
-          tc_fence_before();
-          mbar_arrive(&bars[B_SEMPTY + buf]);
+      const bool open_tile = C::kSpec && tok0 + kTileTokens - 1 <= L - n;
+      // query i of the segment sees tokens <= L - n + i, i.e. row r = i*G + h is visible iff r >= G*(tok-L+n)
+      const int d = tok - (L - n);
+      const int rmin = d > 0 ? d * G : 0;
+      auto load_scores = [&](auto hr_c) {   // (kSpec) unscaled scores, masked unless the tile is open
+        constexpr int HR = decltype(hr_c)::value;
+        tmem_ld_cols<HR>(t_lane + buf * NP + rb, s);
+        if (!open_tile) {
 #pragma unroll
           for (int i = 0; i < HR; ++i) {
             const int r = rb + i;
-            s[i] = (r >= rmin && r < R) ? s[i] * p.scale_log2 : kNegInf;
+            s[i] = (r >= rmin && r < R) ? s[i] : kNegInf;
           }
-          if (!first) {
-            const float* ms = m_s + rb;
+        }
+      };
+      auto weights = [&](auto hr_c) {   // (kSpec) s <- 2^(s * scale - m); returns the sum of this thread's weights
+        constexpr int HR = decltype(hr_c)::value;
+        const float* nm = negm_s + rb;
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        float2 sum = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int r = 0; r < HR; r += 4) {
-              const float4 m4 = *reinterpret_cast<const float4*>(ms + r);
-              need |= (s[r] > m4.x + kRescaleLog2) | (s[r + 1] > m4.y + kRescaleLog2) |
-                      (s[r + 2] > m4.z + kRescaleLog2) | (s[r + 3] > m4.w + kRescaleLog2);
+        for (int r = 0; r < HR; r += 4) {
+          const float4 n4 = *reinterpret_cast<const float4*>(nm + r);
+          const float2 x0 = ffma2(make_float2(s[r], s[r + 1]), sc2, make_float2(n4.x, n4.y));
+          const float2 x1 = ffma2(make_float2(s[r + 2], s[r + 3]), sc2, make_float2(n4.z, n4.w));
+          s[r] = fast_exp2(x0.x);
+          s[r + 1] = fast_exp2(x0.y);
+          s[r + 2] = fast_exp2(x1.x);
+          s[r + 3] = fast_exp2(x1.y);
+          sum = fadd2(sum, fadd2(make_float2(s[r], s[r + 1]), make_float2(s[r + 2], s[r + 3])));
+        }
+        return sum.x + sum.y;
+      };
+      if (alive) {
+        tc_fence_after();
+        with_rows<NP>(nr, [&](auto nr_c) {
+          constexpr int HR = group_rows<NP, decltype(nr_c)::value>();
+          if constexpr (C::kSpec) {
+            load_scores(std::integral_constant<int, HR>{});
+            if (!first) need = weights(std::integral_constant<int, HR>{}) >= kRescaleSum;
+          } else {
+            tmem_ld_cols<HR>(t_lane + buf * NP + rb, s);
+            tc_fence_before();
+            mbar_arrive(&bars[B_SEMPTY + buf]);
+#pragma unroll
+            for (int i = 0; i < HR; ++i) {
+              const int r = rb + i;
+              s[i] = (r >= rmin && r < R) ? s[i] * p.scale_log2 : kNegInf;
+            }
+            if (!first) {
+              const float* ms = m_s + rb;
+#pragma unroll
+              for (int r = 0; r < HR; r += 4) {
+                const float4 m4 = *reinterpret_cast<const float4*>(ms + r);
+                need |= (s[r] > m4.x + kRescaleLog2) | (s[r + 1] > m4.y + kRescaleLog2) |
+                        (s[r + 2] > m4.z + kRescaleLog2) | (s[r + 3] > m4.w + kRescaleLog2);
+              }
             }
           }
         });
@@ -846,46 +908,82 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         if (named_bar_any(bar_id, 128, !alive)) break;
         with_rows<NP>(nr, [&](auto nr_c) {
           constexpr int HR = group_rows<NP, decltype(nr_c)::value>();
+          if constexpr (C::kSpec) {
+            if (!first) load_scores(std::integral_constant<int, HR>{});   // s holds this tile's first weights
+          }
           warp_columns<HR, true>(s, red + (buf * 4 + wq) * NP + rb, lane);
         });
         named_bar_sync(bar_id, 128);
         // row owners: the maximum moves only for rows whose tile maximum passed it by more than the threshold
         if (ct < hr) {
           const int row = rb + ct;
-          float mn = 0.f, alpha = 1.f;
+          float mn = 0.f, neg = -128.f, alpha = 1.f;   // rows past R: no weight
           if (row < R) {
             const float* rr = red + buf * 4 * NP;
-            const float tm = fmaxf(fmaxf(rr[row], rr[NP + row]), fmaxf(rr[2 * NP + row], rr[3 * NP + row]));
+            const float tm = fmaxf(fmaxf(rr[row], rr[NP + row]), fmaxf(rr[2 * NP + row], rr[3 * NP + row])) *
+                             (C::kSpec ? p.scale_log2 : 1.f);   // (kSpec maxima are of unscaled scores)
             const float mo = first ? kNegInf : m_s[row];
             mn = (first || tm > mo + kRescaleLog2) ? fmaxf(mo, tm) : mo;
+            neg = mn == kNegInf ? 0.f : -mn;   // a row that has seen no key yet: masked scores give 2^-inf = 0
             alpha = (mo == kNegInf || mn == mo) ? 1.f : fast_exp2(mo - mn);
           }
           m_s[row] = mn;
+          if constexpr (C::kSpec) negm_s[row] = neg;
           alpha_s[buf * NP + row] = alpha;
         }
         named_bar_sync(bar_id, 128);
       }
       with_rows<NP>(nr, [&](auto nr_c) {
         constexpr int HR = group_rows<NP, decltype(nr_c)::value>();
-        const float* ms = m_s + rb;
-        const float* al = alpha_s + buf * NP + rb;
-#pragma unroll
-        for (int r = 0; r < HR; r += 4) {
-          const float4 m4 = *reinterpret_cast<const float4*>(ms + r);
-          const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
-          float av[4] = {1.f, 1.f, 1.f, 1.f};
+        if constexpr (C::kSpec) {
           if (rescale) {
-            const float4 a4 = *reinterpret_cast<const float4*>(al + r);
-            av[0] = a4.x;
-            av[1] = a4.y;
-            av[2] = a4.z;
-            av[3] = a4.w;
-          }
+            // weights against the new maxima; the running sums scale by alpha
+            weights(std::integral_constant<int, HR>{});
+            const float* al = alpha_s + buf * NP + rb;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float pr = (s[r + i] == kNegInf) ? 0.f : fast_exp2(s[r + i] - mv[i]);
-            l[r + i] = l[r + i] * av[i] + pr;
-            s[r + i] = pr;
+            for (int r = 0; r < HR; r += 4) {
+              const float4 a4 = *reinterpret_cast<const float4*>(al + r);
+              const float2 l0 =
+                  ffma2(make_float2(l[r], l[r + 1]), make_float2(a4.x, a4.y), make_float2(s[r], s[r + 1]));
+              const float2 l1 =
+                  ffma2(make_float2(l[r + 2], l[r + 3]), make_float2(a4.z, a4.w), make_float2(s[r + 2], s[r + 3]));
+              l[r] = l0.x;
+              l[r + 1] = l0.y;
+              l[r + 2] = l1.x;
+              l[r + 3] = l1.y;
+            }
+          } else {
+#pragma unroll
+            for (int r = 0; r < HR; r += 2) {
+              const float2 l0 = fadd2(make_float2(l[r], l[r + 1]), make_float2(s[r], s[r + 1]));
+              l[r] = l0.x;
+              l[r + 1] = l0.y;
+            }
+          }
+          // S(jj) is no longer read: its buffer may take S(jj + 2)
+          tc_fence_before();
+          mbar_arrive(&bars[B_SEMPTY + buf]);
+        } else {
+          const float* ms = m_s + rb;
+          const float* al = alpha_s + buf * NP + rb;
+#pragma unroll
+          for (int r = 0; r < HR; r += 4) {
+            const float4 m4 = *reinterpret_cast<const float4*>(ms + r);
+            const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+            float av[4] = {1.f, 1.f, 1.f, 1.f};
+            if (rescale) {
+              const float4 a4 = *reinterpret_cast<const float4*>(al + r);
+              av[0] = a4.x;
+              av[1] = a4.y;
+              av[2] = a4.z;
+              av[3] = a4.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float pr = (s[r + i] == kNegInf) ? 0.f : fast_exp2(s[r + i] - mv[i]);
+              l[r + i] = l[r + i] * av[i] + pr;
+              s[r + i] = pr;
+            }
           }
         }
         // ---- fold the previous tile's O
@@ -909,6 +1007,27 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           }
         };
         if constexpr (C::kPBuf == 1) fold_prev();   // one P buffer: PV(jj-1) must finish before P is rewritten
+        if constexpr (C::kOAcc) {
+          // P(jj) goes into the buffer PV(jj-2) read.  A tile that moved some row maxima first scales the group's O
+          // rows by alpha, once PV(jj-1) has added onto them; PV(jj) then adds this tile's P on top.
+          if (rescale && !first && alive) {
+            alive = mbar_wait_warp(&bars[ofull_bar(pbuf(jj - 1))], pphase(jj - 1), abort);
+            if (alive) {
+              tc_fence_after();
+              const float* ap = alpha_s + buf * NP + rb;
+#pragma unroll
+              for (int c = 0; c < HR; c += 8) {   // eight columns at a time: few registers next to P and l
+                float ot[8];
+                tmem_ld8(t_lane + (2 + ob) * NP + rb + c, ot);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) ot[i] *= ap[c + i];
+                tmem_st8(t_lane + (2 + ob) * NP + rb + c, ot);
+              }
+              tc_fence_before();
+            }
+          }
+          if (jj >= 2 && alive) alive = mbar_wait_warp(&bars[ofull_bar(pbuf(jj))], pphase(jj - 2), abort);
+        }
         // ---- rows past the sequence end may hold stale or uninitialised values: zero V there so P = 0 cannot
         // meet a NaN in the PV product (last tile of a sequence; group 0, before its P arrival)
         if (alive && wg == 0 && L - tok0 < kTileTokens) {
@@ -924,8 +1043,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         }
         // ---- P^T (bf16) into its buffer, MN-major without swizzle: 8 consecutive rows of token ct form one 16-byte
         // vector.  Rows past NR (up to the UMMA N) are never read back: their O^T columns are ignored.  The buffer's
-        // last reader has finished: its O was folded before this point (PV(jj-1) just above with one buffer;
-        // PV(jj-2) at tile jj-1 or at the end of its segment with two).
+        // last reader has finished: PV(jj-1) was folded just above with one buffer; with two, PV(jj-2) was waited for
+        // above (O in TMEM) or folded at tile jj-1 or at the end of its segment.
         if (alive) {
           uint8_t* pb = p_smem + pbuf(jj) * NP * 256 + ct * 16 + (rb >> 3) * 2048;
 #pragma unroll
@@ -940,20 +1059,25 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           fence_proxy_async_smem();
           mbar_arrive(&bars[pfull_bar(pbuf(jj))]);
         }
-        if constexpr (C::kPBuf == 2) fold_prev();   // the fold waits for PV(jj-1) after this tile's P is handed off
+        // two P buffers, O in registers: the fold waits for PV(jj-1) after this tile's P is handed off
+        if constexpr (C::kPBuf == 2 && !C::kOAcc) fold_prev();
         if (last && alive) {
           alive = mbar_wait_warp(&bars[ofull_bar(pbuf(jj))], pphase(jj), abort);
           if (alive) {
             tc_fence_after();
-            const float* ap = alpha_s + buf * NP + rb;
-            float ot[HR];
-            tmem_ld_cols<HR>(t_lane + (2 + pbuf(jj)) * NP + rb, ot);
-            if (rescale) {
-#pragma unroll
-              for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
+            if constexpr (C::kOAcc) {
+              tmem_ld_cols<HR>(t_lane + (2 + ob) * NP + rb, o);   // the segment's accumulated O
             } else {
+              const float* ap = alpha_s + buf * NP + rb;
+              float ot[HR];
+              tmem_ld_cols<HR>(t_lane + (2 + pbuf(jj)) * NP + rb, ot);
+              if (rescale) {
 #pragma unroll
-              for (int i = 0; i < HR; ++i) o[i] += ot[i];
+                for (int i = 0; i < HR; ++i) o[i] = o[i] * ap[i] + ot[i];
+              } else {
+#pragma unroll
+                for (int i = 0; i < HR; ++i) o[i] += ot[i];
+              }
             }
             tc_fence_before();
             warp_columns<HR, false>(l, lred + wq * NP + rb, lane);
@@ -1015,15 +1139,16 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   }
 }
 
-template <int NP>
+template <int NP, bool Spec = false>
 cudaError_t launch_np(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const DecodeParams& p, int grid,
                       cudaStream_t stream, bool pdl) {
-  constexpr int smem = Cfg<NP>::kBytes;
+  constexpr int smem = Cfg<NP, Spec>::kBytes;
   static_assert(smem <= 232448, "shared memory budget");
-  cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e =
+      cudaFuncSetAttribute(paged_decode_kernel<NP, Spec>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  return launch_kernel(paged_decode_kernel<NP>, dim3(grid), dim3(Cfg<NP>::kThreads), smem, stream, pdl, tm_k, tm_v,
-                       p);
+  return launch_kernel(paged_decode_kernel<NP, Spec>, dim3(grid), dim3(Cfg<NP, Spec>::kThreads), smem, stream, pdl,
+                       tm_k, tm_v, p);
 }
 
 }  // namespace
@@ -1060,7 +1185,10 @@ cudaError_t launch_paged_decode(const CUtensorMap& tm_k, const CUtensorMap& tm_v
   switch (np) {
     case 16: return launch_np<16>(tm_k, tm_v, p, grid, stream, pdl);
     case 32: return launch_np<32>(tm_k, tm_v, p, grid, stream, pdl);
-    case 48: return launch_np<48>(tm_k, tm_v, p, grid, stream, pdl);
+    // fixed-length batches of 33-48 rows (verify with many drafts) take the speculative-weights variant; varlen
+    // calls, whose short runs are mostly 1-row decode segments, the plain one
+    case 48: return p.cu_q == nullptr ? launch_np<48, true>(tm_k, tm_v, p, grid, stream, pdl)
+                                      : launch_np<48>(tm_k, tm_v, p, grid, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -69,6 +69,7 @@ extern "C" NVA_API int nva_paged_decode_noalloc(const void* q, int64_t q_row_str
   // the same argument checks as nva_paged_decode
   if (num_seqs < 0 || q_per_seq < 1 || num_heads <= 0 || num_kv_heads <= 0) return NVA_ERR_INVALID_ARGUMENT;
   if (num_heads % num_kv_heads != 0) return NVA_ERR_INVALID_ARGUMENT;
+  if (!(softmax_scale > 0.f && softmax_scale < 3.0e38f)) return NVA_ERR_INVALID_ARGUMENT;   // positive, finite
   if (head_dim != nva::kHeadDim) return NVA_ERR_UNSUPPORTED;
   if (num_seqs == 0) return NVA_OK;
   if (num_seqs > nva::kMaxDecodeSeqs) return NVA_ERR_UNSUPPORTED;

@@ -53,6 +53,14 @@ def test_invalid_arguments_rejected_on_host():
     assert lib.nva_paged_decode(0, 0, 0, 0, 1, 256, 0, 0, 1, 1, 1, 30, 8, 128, 1.0, 0, 0, 0, 0, 0) == 1
     # block size not a multiple of 128
     assert lib.nva_paged_decode(16, 4096, 16, 16, 1, 100, 16, 16, 1, 1, 1, 32, 8, 128, 1.0, 16, 4096, 16, 1 << 30, 0) == 2
+    # the softmax scale must be positive and finite (decode, varlen, no-workspace decode)
+    for bad in (0.0, -0.088, float("nan"), float("inf")):
+        assert lib.nva_paged_decode(16, 4096, 16, 16, 1, 256, 16, 16, 1, 1, 1, 32, 8, 128, bad, 16, 4096, 16,
+                                    1 << 30, 0) == 1
+        assert lib.nva_varlen_attention(16, 4096, 0, 0, 0, 0, 16, 16, 1, 256, 16, 16, 1, 1, 1, 1, 1, 16, 1, 32, 8,
+                                        128, bad, 16, 4096, 16, 1 << 30, 0) == 1
+        assert lib.nva_paged_decode_noalloc(16, 4096, 16, 16, 1, 256, 16, 16, 1, 1, 1, 32, 8, 128, bad, 16, 4096,
+                                            0) == 1
     # 64 draft tokens x 4 heads does not fit the 48-row tile
     assert lib.nva_paged_decode(16, 4096, 16, 16, 1, 256, 16, 16, 1, 1, 16, 32, 8, 128, 1.0, 16, 4096, 16, 1 << 30, 0) == 2
     # greedy accept: bad id width, negative k

@@ -72,6 +72,14 @@ def test_verify(cuda, k):
     assert_attn_close(run_decode(b), ref_decode(b), f"verify k={k}")
 
 
+@pytest.mark.parametrize("lens", [[9], [127], [128, 136], [137, 263], [264, 265], [383, 384, 385]])
+def test_verify_k8_tile_edges(cuda, lens):
+    """k = 8 (36 rows, the 48-row variant) where the last draft position's visible range ends at, just before and
+    just after a 128-key tile edge: tiles every row sees in full take the unmasked path, the rest the masked one."""
+    b = batch(lens, n=9, seed=len(lens) + lens[0])
+    assert_attn_close(run_decode(b), ref_decode(b), f"k=8 tile edges {lens}")
+
+
 @pytest.mark.parametrize("k", [1, 2, 4, 8])
 def test_verify_config3_full(cuda, k):
     """B=32, context U[256, 2048], k+1 causal queries per sequence."""
@@ -80,11 +88,12 @@ def test_verify_config3_full(cuda, k):
     assert_attn_close(run_decode(b), ref_decode(b), f"config3 k={k}")
 
 
-@pytest.mark.parametrize("n", [1, 5])
+@pytest.mark.parametrize("n", [1, 5, 9, 12])
 def test_rising_scores_rescale_and_merge(cuda, n):
     """Scores that rise along the keys (dim 0 of every query is 4, dim 0 of key p gains 0.3 p: ~9.8 in log2 units
     per 64 keys): every tile moves the row maxima past the 2^8 rescale threshold, and the pieces of a split sequence
-    reach the in-kernel merge with log-sum-exps hundreds of log2 units apart."""
+    reach the in-kernel merge with log-sum-exps hundreds of log2 units apart.  n = 9 and 12 (36 and 48 rows) run the
+    48-row variant whose O stays in TMEM: every tile there scales the accumulated O by alpha before its PV product."""
     lens = [2000, 700, 129, 4000]
     b = batch(lens, n=n, seed=41)
     for i, L in enumerate(lens):
@@ -95,23 +104,25 @@ def test_rising_scores_rescale_and_merge(cuda, n):
     assert_attn_close(run_decode(b), ref_decode(b), f"rising scores n={n}")
 
 
-def test_padding_sequences_zero_and_invariant(cuda):
+@pytest.mark.parametrize("n", [3, 9])
+def test_padding_sequences_zero_and_invariant(cuda, n):
     """Padded sequences (length 0, table -1) output zeros, and real rows are bitwise identical with and without
     the padding (the check_padding.py property that eager == CUDA-graph runs rely on)."""
     lens = [300, 1200, 4000]
-    a = batch(lens, n=3, seed=3)
-    p = batch(lens, n=3, seed=3, pad_seqs=13)
+    a = batch(lens, n=n, seed=3)
+    p = batch(lens, n=n, seed=3, pad_seqs=13)
     oa = run_decode(a)
     op = run_decode(p)
     assert torch.equal(oa, op[:3])
     assert op[3:].abs().sum() == 0
 
 
-def test_stale_nan_past_context_is_ignored(cuda):
+@pytest.mark.parametrize("n", [2, 9])
+def test_stale_nan_past_context_is_ignored(cuda, n):
     """Cache rows past a sequence's length inside its last block may hold anything (torch.empty pool, rejected
     drafts); they must not leak into the output."""
     lens = [100, 300, 129]
-    b = batch(lens, n=2, seed=4)
+    b = batch(lens, n=n, seed=4)
     ref = ref_decode(b)
     for i, L in enumerate(lens):
         nblk = (L + 255) // 256
@@ -121,11 +132,12 @@ def test_stale_nan_past_context_is_ignored(cuda):
     assert_attn_close(run_decode(b), ref, "nan tail")
 
 
-def test_cuda_graph_replay_matches_eager(cuda):
+@pytest.mark.parametrize("n", [5, 12])
+def test_cuda_graph_replay_matches_eager(cuda, n):
     from nvattn import ops
-    b = batch([513, 77, 2048, 1], n=5, seed=6)
+    b = batch([513, 77, 2048, 1], n=n, seed=6)
     eager = run_decode(b)
-    B, n, H, D = b.num_seqs, 5, 32, 128
+    B, H, D = b.num_seqs, 32, 128
     q_static = b.q.view(B, n, H, D).clone()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -175,7 +187,7 @@ def test_kernels_match_flash_attn_golden(cuda, name):
     assert_attn_close(got, fa2_out.float(), f"kernels vs flash-attn: {name}")
 
 
-@pytest.mark.parametrize("pieces_case", ["two_pieces", "table", "many_pieces"])
+@pytest.mark.parametrize("pieces_case", ["two_pieces", "table", "many_pieces", "wide_two_pieces"])
 def test_merge_tickets_left_zero_and_repeatable(cuda, pieces_case):
     """The workspace contract: the merge tickets (first block of the workspace) are zero again after every call,
     whichever merge path ran (two pieces, the weight table for 3..16 pieces, the plain loop beyond), and repeated
@@ -184,8 +196,10 @@ def test_merge_tickets_left_zero_and_repeatable(cuda, pieces_case):
     from nvattn.workloads import varlen_batch
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     ticket_bytes = (2 * sms * 4 + 255) // 256 * 256
-    lens = {"two_pieces": [1500] * 40, "table": [2048 * 3] * 4, "many_pieces": [4096]}[pieces_case]
-    b = batch(lens, n=3 if pieces_case == "two_pieces" else 1, NB=512, seed=21)
+    lens = {"two_pieces": [1500] * 40, "table": [2048 * 3] * 4, "many_pieces": [4096],
+            "wide_two_pieces": [1500] * 40}[pieces_case]
+    n = {"two_pieces": 3, "wide_two_pieces": 10}.get(pieces_case, 1)   # (10 x 4 rows: the 48-row variant)
+    b = batch(lens, n=n, NB=512, seed=21)
     first = run_decode(b).clone()
     ws = ops._WORKSPACES[torch.cuda.current_device()]
     torch.cuda.synchronize()
