@@ -825,7 +825,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         // (two groups: always two P buffers)
         if (jj >= 2) alive = alive && mbar_wait_warp(&bars[ofull_bar(pbuf(jj))], pphase(jj - 2), abort);
         if (alive) mbar_arrive(&bars[pfull_bar(pbuf(jj))]);
-        if (named_bar_any(bar_id, 128, !alive)) break;
+        // A warp whose descriptor wait gave up decides padding vs working rows from the previous segment's R, so on
+        // the way out this path mirrors the working path's two votes (the rescale vote, then the "gave up" vote):
+        // whichever path each warp of the group took, their barrier arrivals pair up and all leave together.
+        if (named_bar_any(bar_id, 128, !alive)) {
+          named_bar_any(bar_id, 128, true);
+          break;
+        }
         continue;
       }
       // ---- S tile -> weights.  Row maxima are lazy: the weights P = 2^(s * scale - m) are taken against each row's
