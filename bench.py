@@ -402,7 +402,9 @@ def e2e_model_rows(args):
     n-gram speculative decoding with dynamic k over a fixed injected step-cost table, 64 requests of 1024 prompt
     tokens, 256 new tokens each; the reference arm (its flash-attn 2.8.3 + Triton scatter) and this package's full
     drop-in (attention, fused q/k-norm + rotary + scatter prologue, sharded greedy verify), each in its own process,
-    one after the other.  Output tokens / generate() wall time.  With random weights the model does not repeat its
+    one after the other.  Output tokens / generate() wall time, after the reference bench's warm-up and one more on
+    requests of the measured shape (other ids), so that first calls at the measured batch sizes (torch.compile work)
+    stay outside the timed call in both arms.  With random weights the model does not repeat its
     own text, so n-gram guesses rarely fire; the second pair of rows lets the model guess for itself (every decode
     step a k = 4 verify step, ~93% of guesses accepted)."""
     import tempfile
@@ -416,7 +418,7 @@ def e2e_model_rows(args):
             for arm in ("reference", "nvattn+all"):
                 out = os.path.join(tmp, f"{variant}_{arm}.json")
                 cmd = [sys.executable, "-m", "nvattn.e2e", "--arm", arm, "--variant", variant, "--model-dir", model,
-                       "--out", out] + extra
+                       "--out", out, "--shape-warmup"] + extra
                 try:
                     r = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
                 except subprocess.TimeoutExpired:

@@ -263,9 +263,13 @@ def install_proposer(llm, kind: str, prompts: list[list[int]], replay: list[list
 
 def run_arm(arm: str, variant: str, prompts: list[list[int]], max_tokens: int, model_path: str, tp: int = 1,
             step_costs_file: str | None = None, save_step_costs: str | None = None, weight_seed: int = 0,
-            proposer: str = "ngram", replay: list[list[int]] | None = None, **engine_overrides) -> dict:
+            proposer: str = "ngram", replay: list[list[int]] | None = None,
+            shape_warmup: list[list[int]] | None = None, **engine_overrides) -> dict:
     """One engine run in this process: build LLM(model_path, ...) with the arm's attention, generate greedily
-    (ignore_eos, exactly max_tokens per request) and return tokens, timing and speculative-decoding counters."""
+    (ignore_eos, exactly max_tokens per request) and return tokens, timing and speculative-decoding counters.
+    `shape_warmup`: requests shaped like the measured ones (other ids, so no prefix-cache block is shared), run for
+    32 new tokens before the measurement, so that the first calls at the measured batch sizes (torch.compile of the
+    sampler and norms for those shapes) happen outside the timed generate()."""
     assert arm in ARMS, arm
     os.environ[ENV_ARM], os.environ[ENV_TP], os.environ[ENV_SEED] = arm, str(tp), str(weight_seed)
     if step_costs_file:
@@ -294,7 +298,7 @@ def run_arm(arm: str, variant: str, prompts: list[list[int]], max_tokens: int, m
     # of the sampler and norms, kernel setup), so one request, then four of 64-256 tokens, 32 new tokens each; their
     # tokens share no prefix-cache block with the measured prompts.  Counters are reset after it.
     warm = [[100 + i % (3 + j) for i in range(64 * (j + 1))] for j in range(4)]
-    for batch in (warm[:1], warm):
+    for batch in (warm[:1], warm) + ((shape_warmup,) if shape_warmup else ()):
         llm.generate(batch, SamplingParams(temperature=0, max_tokens=32, ignore_eos=True), use_tqdm=False)
     llm.reset_spec_stats()
     llm.num_mixed_steps = 0
@@ -343,6 +347,8 @@ def main(argv=None) -> None:
     p.add_argument("--replay-from", default=None, help="--proposer replay: a result JSON of a plain greedy run")
     p.add_argument("--max-num-seqs", type=int, default=None)
     p.add_argument("--gpu-memory-utilization", type=float, default=None)
+    p.add_argument("--shape-warmup", action="store_true",
+                   help="also warm up on requests of the measured shape (prompt seed + 1, 32 new tokens)")
     p.add_argument("--out", required=True)
     a = p.parse_args(argv)
     import tempfile
@@ -362,9 +368,11 @@ def main(argv=None) -> None:
     if a.replay_from:
         with open(a.replay_from) as f:
             replay = json.load(f)["tokens"]
+    shape_warmup = config5_prompts(a.num_prompts, a.prompt_len, seed=a.seed + 1) if a.shape_warmup else None
     res = run_arm(a.arm, a.variant, prompts, a.max_tokens, model_path, a.tp, a.step_costs, a.save_step_costs,
-                  a.weight_seed, a.proposer, replay, **overrides)
+                  a.weight_seed, a.proposer, replay, shape_warmup, **overrides)
     res["prompts_seed"], res["num_prompts"], res["prompt_len"] = a.seed, a.num_prompts, a.prompt_len
+    res["shape_warmup"] = bool(shape_warmup)
     with open(a.out, "w") as f:
         json.dump(res, f)
     print(json.dumps({k: v for k, v in res.items() if k != "tokens"}))
