@@ -21,12 +21,17 @@
 //       boxes into rings (3 stages at 16 rows, 2 at 32/48); K slots are released right after S = K Q^T, V slots
 //       after the PV product.  They start before the TMEM allocation and leave when done; the other warps meet on
 //       named barrier 3;
-//   1 = TMEM owner + UMMA issuer: products in a fixed order, QK(0), QK(1), then PV(j), QK(j+2), ... (S, P and O
-//       buffers are reused by tile parity, so this order is what keeps every barrier within one phase);
+//   1 = TMEM owner + UMMA issuer: products in a fixed order, QK(0), QK(1), then PV(j), QK(j+2), ... (S and P
+//       buffers, and O except in the speculative-weights variant, are reused by tile parity, so this order is what
+//       keeps every barrier within one phase);
 //   2 = Q loader: gathers a segment's rows into the swizzled operand layout (cp.async, zero-filled padding);
 //   4..7 (and 8..11) = softmax: thread ct of a warpgroup owns TMEM lane ct (token ct of S^T, dim ct of O^T).
 //       Column maxima and sums over the 128 tokens use a transposed butterfly (each shuffle stage halves the rows
 //       a lane carries).  With two warpgroups each takes half of the rows; rows never interact in the softmax.
+//
+// Fixed-length batches of 33-48 rows (verify with 8 or more drafts) run a speculative-weights variant of the 48-row
+// instantiation: unscaled scores, no mask on tiles every row sees in full, the weights taken before the rescale vote
+// (packed FP32) and voted on by their sum, and the O accumulator kept in TMEM across a segment's tiles.
 #include <type_traits>
 
 #include "nva_ptx.cuh"
