@@ -166,10 +166,12 @@ def decode_strong_shard(world, rank, seed=0):
 
 
 def decode_kernel_name(n, H, KVH):
-    """The paged_decode_kernel<NP> instantiation a decode / verify call runs: the packed rows q_per_seq x group of
-    one kv head, padded to 16, 32 or 48 (decode_rows_padded in csrc/paged_decode.cu)."""
+    """The paged_decode_kernel<NP, Spec> instantiation a decode / verify call (fixed-length batch) runs, as profilers
+    name it: the packed rows q_per_seq x group of one kv head, padded to 16, 32 or 48 (decode_rows_padded in
+    csrc/paged_decode.cu); Spec = 1, the speculative-weights variant, at 48 rows."""
     rows = n * (H // KVH)
-    return f"paged_decode_kernel<{next(x for x in (16, 32, 48) if rows <= x)}>"
+    np_ = next(x for x in (16, 32, 48) if rows <= x)
+    return f"paged_decode_kernel<{np_}, {1 if np_ == 48 else 0}>"
 
 
 def attn_bytes(lens, n, H, KVH):
